@@ -1,0 +1,463 @@
+#!/usr/bin/env python
+"""Benchmark of the GDN decode hot path on B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+
+Workloads (the default is the one the headline metric is quoted on):
+  decode  config 2: indexed decode, 256 sequences per GPU, T=1, pool of 1024 fp32 slots [32,128,128]
+  verify  config 3: MTP verify, 64 sequences per GPU, T=4, accepted ~ U{1..4}
+  copy    config 4: gather 512 slots of a 2048-slot layer pool, scatter them to a permuted set
+A step is one launch of the op over that batch.  Under torchrun every rank runs the same
+per-GPU workload on its own slot shard (weak scaling, no data-path collective); the
+rank-local device times are combined as their maximum.  Rank 0 prints one JSON line.
+
+--impl reference times the CPU oracle port (oracle/, all host threads) on the same workload and
+metric; under torchrun only rank 0 runs it.
+"""
+
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+METRIC = "GDN decode tokens/s and state HBM GB/s (% of 8 TB/s) at 1/2/4/8 B200"
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+L2_BYTES = 126 * 1024 * 1024
+
+
+# ---------------------------------------------------------------------------------------------
+# process setup
+# ---------------------------------------------------------------------------------------------
+def parse_args(argv=None):
+    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=4000)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--workload", choices=("decode", "verify", "copy"), default="decode")
+    p.add_argument("--e2e-steps", type=int, default=200)
+    p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline budget (rank 0, N=1)")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    args = p.parse_args(argv)
+    if args.warmup < 3:
+        p.error("--warmup must be at least 3")
+    if args.steps < 1:
+        p.error("--steps must be positive")
+    return args
+
+
+class Dist:
+    """Rank bookkeeping; a gloo group carries the host barriers and the max-over-ranks timing."""
+
+    def __init__(self, gpus: int):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        if self.world != gpus:
+            raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={self.world}: launch N>1 under torchrun")
+        self.group = None
+        if self.world > 1:
+            import torch.distributed as dist
+
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            dist.init_process_group("gloo", rank=self.rank, world_size=self.world, timeout=timedelta(seconds=120))
+            self.group = dist
+
+    def barrier(self):
+        if self.group is not None:
+            self.group.barrier()
+
+    def max(self, value: float) -> float:
+        if self.group is None:
+            return value
+        import torch
+
+        t = torch.tensor([value], dtype=torch.float64)
+        self.group.all_reduce(t, op=self.group.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, value: float) -> float:
+        if self.group is None:
+            return value
+        import torch
+
+        t = torch.tensor([value], dtype=torch.float64)
+        self.group.all_reduce(t, op=self.group.ReduceOp.SUM)
+        return float(t.item())
+
+    def close(self):
+        if self.group is not None:
+            self.group.destroy_process_group()
+
+
+def measured_peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": float(data["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": FALLBACK_HBM_GBS, "source": "fallback"}
+
+
+def ncu_traffic(workload: str):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
+    path = ROOT / "profiles" / "ncu_traffic.json"
+    if not path.exists():
+        return None
+    entry = json.loads(path.read_text()).get(workload)
+    return None if entry is None else entry.get("bytes_per_launch")
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling around the timed region."""
+
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.window = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def mark(self, start: float, end: float):
+        self.window = (start, end)
+
+    def summary(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = []
+        for rec in csv.reader(io.StringIO(out)):
+            if len(rec) < 10:
+                continue
+            rec = [r.strip() for r in rec]
+            try:
+                stamp = time.mktime(time.strptime(rec[0].split(".")[0], "%Y/%m/%d %H:%M:%S"))
+                stamp += float("0." + rec[0].split(".")[1]) if "." in rec[0] else 0.0
+                rows.append((stamp, float(rec[2]), float(rec[3]), rec[5], rec[6:10]))
+            except (ValueError, IndexError):
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        start, end = self.window if self.window else (rows[0][0], rows[-1][0])
+        inside = [r for r in rows if start - 0.15 <= r[0] <= end + 0.15]
+        scope = "timed region"
+        if not inside:
+            inside, scope = rows, "whole run (timed region shorter than the 100 ms sampling interval)"
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in inside for i, v in enumerate(r[4]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[1] for r in inside), "sm_max_mhz": max(r[2] for r in inside),
+                "reasons": reasons, "samples": len(inside), "scope": scope}
+
+
+# ---------------------------------------------------------------------------------------------
+# our implementation
+# ---------------------------------------------------------------------------------------------
+def timed_launches(fn, steps: int, warmup: int, dist: Dist, stream):
+    """W untimed calls, then K timed calls bracketed by barrier + synchronize; per-launch events."""
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    begin, finish = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wall0 = time.time()
+    begin.record(stream)
+    for i in range(steps):
+        starts[i].record(stream)
+        fn()
+        ends[i].record(stream)
+    finish.record(stream)
+    torch.cuda.synchronize()
+    wall1 = time.time()
+    dist.barrier()
+    total_ms = begin.elapsed_time(finish)
+    launch_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    return total_ms, launch_ms, (wall0, wall1)
+
+
+def run_ours(args, dist: Dist) -> dict | None:
+    import torch
+
+    from lightdelta_b200 import ops  # noqa: F401
+    from lightdelta_b200 import workloads
+
+    torch.cuda.set_device(dist.local_rank)
+    device = torch.device("cuda", dist.local_rank)
+    stream = torch.cuda.current_stream(device)
+    sampler = ClockSampler(device.index if device.index is not None else 0)
+    peaks = measured_peaks()
+    seed = 1000 * dist.rank
+
+    if args.workload in ("decode", "verify"):
+        case = workloads.config2(device, seed=2 + seed) if args.workload == "decode" else workloads.config3(
+            device, seed=3 + seed)
+        op_args = case.op_args()
+        requests, width = case.slots.shape
+        tokens = case.tokens
+        hv, h = case.num_v_heads, case.num_k_heads
+        bytes_per_launch = workloads.decode_algorithmic_bytes(requests, width, tokens, h, hv)
+        touched = requests * (1 + width) * hv * workloads.SLOT_HEAD_BYTES
+
+        def fn():
+            torch.ops.lightdelta.decode(*op_args)
+
+        units_per_step, unit = tokens, "tokens/s"
+        config = {"workload": f"config{'2' if args.workload == 'decode' else '3'}_{args.workload}",
+                  "sequences_per_gpu": requests, "tokens_per_sequence": width, "num_k_heads": h,
+                  "num_v_heads": hv, "head_dim": 128, "pool_slots": case.pool.shape[0],
+                  "state_dtype": "fp32", "activation_dtype": "bf16"}
+    else:
+        pool = torch.empty(2048, 32, 128, 128, device=device)
+        pool.normal_(0.0, 0.02)
+        gather_idx, scatter_idx = workloads.config4_indices(device, seed=4 + seed)
+        packed = torch.empty(512, 32, 128, 128, device=device)
+        valid = torch.ones(512, device=device, dtype=torch.bool)
+
+        def fn():
+            torch.ops.lightdelta.gather_state(pool, gather_idx, valid, packed)
+            torch.ops.lightdelta.scatter_state(packed, scatter_idx, pool)
+
+        bytes_per_launch = 512 * 32 * workloads.SLOT_HEAD_BYTES * 2  # per op: read + write 512 slots
+        touched = bytes_per_launch * 2
+        units_per_step, unit = 512, "slots/s"
+        config = {"workload": "config4_copy", "pool_slots": 2048, "slots_per_step": 512,
+                  "ops_per_step": ["gather_state", "scatter_state"], "num_v_heads": 32, "head_dim": 128}
+
+    total_ms, launch_ms, window = timed_launches(fn, args.steps, args.warmup, dist, stream)
+    sampler.mark(*window)
+    clocks = sampler.summary()
+    max_ms = dist.max(total_ms)
+    launches_per_step = 2 if args.workload == "copy" else 1
+    kernel_ms = launch_ms / launches_per_step  # copy: two equal-size copies per step
+    achieved_gbs = bytes_per_launch / (kernel_ms * 1e-3) / 1e9
+    value = units_per_step * args.steps * dist.world / (max_ms * 1e-3)
+    state_gbs_total = dist.sum(bytes_per_launch * launches_per_step * args.steps / (total_ms * 1e-3) / 1e9)
+
+    e2e = None
+    if args.workload in ("decode", "verify"):
+        e2e = run_e2e(case, args, dist, stream)
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline and args.workload in ("decode", "verify"):
+        cpu = cpu_baseline(case, args.cpu_seconds)
+
+    if dist.rank != 0:
+        return None
+    traffic = ncu_traffic(args.workload)
+    return {
+        "metric": METRIC,
+        "value": value,
+        "unit": unit,
+        "n_gpus": dist.world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": max_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp32" if args.workload != "copy" else "fp32 (bit copy)",
+        "data": "synthetic (seeded, BASELINE config shapes and distributions)",
+        "impl": "ours",
+        "config": {**config, "parallelism": f"slot-sharded x{dist.world}, no collective",
+                   "l2": f"no flush: the {touched / 1e9:.2f} GB touched per step exceeds the 126 MB L2"},
+        "state_gbs": state_gbs_total,
+        "hbm_frac_of_8tbs_per_gpu": state_gbs_total / dist.world / NOMINAL_HBM_GBS,
+        "roofline": {
+            "bound": "hbm",
+            "achieved": achieved_gbs,
+            "peak": peaks["hbm_gbs"],
+            "unit": "GB/s",
+            "frac": achieved_gbs / peaks["hbm_gbs"],
+            "peak_source": peaks["source"],
+            "traffic": traffic,
+            "algorithmic_bytes_per_launch": bytes_per_launch,
+            "kernel_ms": kernel_ms,
+        },
+        "e2e": e2e,
+        "cpu_baseline": cpu,
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks,
+    }
+
+
+def run_e2e(case, args, dist: Dist, stream) -> dict:
+    """Same metric through the public op with host buffers: pinned H2D of the step's activations and
+    request metadata, the op, and a D2H read of the output, all inside the timed region."""
+    import torch
+
+    proj_d = case.qkv.as_strided((case.tokens, case.qkv.stride(0)), (case.qkv.stride(0), 1))
+    ba_d = case.b.as_strided((case.tokens, case.b.stride(0)), (case.b.stride(0), 1))
+    host = {name: t.cpu().pin_memory() for name, t in
+            (("proj", proj_d), ("ba", ba_d), ("slots", case.slots), ("cu", case.cu), ("accepted", case.accepted))}
+    out_h = torch.empty(case.out.shape, dtype=case.out.dtype).pin_memory()
+    device_bufs = {"proj": proj_d, "ba": ba_d, "slots": case.slots, "cu": case.cu, "accepted": case.accepted}
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = out_h.numel() * out_h.element_size()
+    op_args = case.op_args()
+
+    def step():
+        for name, t in host.items():
+            device_bufs[name].copy_(t, non_blocking=True)
+        torch.ops.lightdelta.decode(*op_args)
+        out_h.copy_(case.out, non_blocking=True)
+
+    steps = min(args.e2e_steps, args.steps)
+    total_ms, _, _ = timed_launches(step, steps, args.warmup, dist, stream)
+    max_ms = dist.max(total_ms)
+    return {"value": case.tokens * steps * dist.world / (max_ms * 1e-3), "unit": "tokens/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
+            "api": "torch.ops.lightdelta.decode with pinned host inputs/outputs"}
+
+
+# ---------------------------------------------------------------------------------------------
+# CPU baseline / reference arm (the oracle port; never the product path)
+# ---------------------------------------------------------------------------------------------
+def host_workload(case, requests: int | None = None):
+    """Host copy of a decode case restricted to `requests` sequences, with the pool compacted to
+    the slots they use (slot 0 kept as the null slot)."""
+    import numpy as np
+    import torch
+
+    R, W = case.slots.shape
+    r = R if requests is None else max(1, min(R, requests))
+    slots = case.slots[:r].cpu().numpy()
+    used = sorted(set(slots.flatten().tolist()) - {0})
+    remap = {s: i + 1 for i, s in enumerate(used)}
+    pool = case.pool[torch.as_tensor([0] + used, device=case.pool.device, dtype=torch.long)].cpu().numpy()
+    tokens = int(case.cu[r].item())
+
+    def bf16(t):
+        return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+    return dict(
+        qkv=bf16(case.qkv[:tokens]), a=bf16(case.a[:tokens]), b=bf16(case.b[:tokens]),
+        a_log=case.a_log.cpu().numpy(), dt_bias=case.dt_bias.cpu().numpy(),
+        slots=np.vectorize(lambda s: remap.get(int(s), 0), otypes=[np.int32])(slots),
+        cu=case.cu[: r + 1].cpu().numpy(), accepted=case.accepted[:r].cpu().numpy(), pool=pool,
+        gate=bf16(case.gate[:tokens]), weight=bf16(case.weight), out=np.zeros((tokens, case.num_v_heads, 128), np.uint16),
+        num_k_heads=case.num_k_heads, tokens=tokens, requests=r,
+    )
+
+
+def oracle_step(w):
+    import oracle
+
+    oracle.decode(w["qkv"], w["a"], w["b"], w["a_log"], w["dt_bias"], w["slots"], w["cu"], w["accepted"], w["pool"],
+                  w["gate"], w["weight"], w["out"], num_k_heads=w["num_k_heads"], threads=w["threads"])
+
+
+def cpu_baseline(case, seconds: float) -> dict:
+    import oracle
+
+    w = host_workload(case)
+    w["threads"] = oracle.default_threads()
+    oracle_step(w)  # warm-up
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        oracle_step(w)
+        reps += 1
+        elapsed = time.perf_counter() - t0
+        if elapsed >= seconds:
+            break
+    return {"value": w["tokens"] * reps / elapsed, "unit": "tokens/s", "cores": w["threads"], "kind": "port",
+            "sample": f"full batch ({w['requests']} sequences, {w['tokens']} tokens) x {reps} repetitions, "
+                      f"{elapsed:.1f} s, C oracle with OpenMP"}
+
+
+def run_reference(args, dist: Dist) -> dict | None:
+    if dist.rank != 0:
+        return None
+    import torch
+
+    import oracle
+    from lightdelta_b200 import workloads
+
+    if args.workload == "copy":
+        return {"impl": "reference", "unavailable": "the copy workload has no CPU arm in this harness"}
+    device = torch.device("cuda", dist.local_rank) if torch.cuda.is_available() else torch.device("cpu")
+    case = workloads.config2(device, seed=2) if args.workload == "decode" else workloads.config3(device, seed=3)
+    threads = oracle.default_threads()
+    # Size each step so that warmup + steps finish in about a minute.
+    probe = host_workload(case, 8)
+    probe["threads"] = threads
+    t0 = time.perf_counter()
+    oracle_step(probe)
+    per_request = (time.perf_counter() - t0) / probe["requests"]
+    budget = 60.0 / (args.steps + args.warmup)
+    requests = max(1, min(case.slots.shape[0], int(budget / max(per_request, 1e-9))))
+    w = host_workload(case, requests)
+    w["threads"] = threads
+    for _ in range(args.warmup):
+        oracle_step(w)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle_step(w)
+    elapsed = time.perf_counter() - t0
+    value = w["tokens"] * args.steps / elapsed
+    sample = (f"{w['requests']} of {case.slots.shape[0]} sequences ({w['tokens']} tokens) per step, "
+              f"C oracle port with OpenMP on {threads} host threads")
+    return {
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": dist.world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": elapsed * 1e3 / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp32",
+        "data": "synthetic (seeded, BASELINE config shapes and distributions)",
+        "impl": "reference",
+        "config": {"workload": f"config{'2' if args.workload == 'decode' else '3'}_{args.workload}",
+                   "sequences_per_gpu": case.slots.shape[0], "tokens_per_sequence": case.slots.shape[1],
+                   "parallelism": "rank 0 host CPU only"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main(argv=None) -> int:
+    args = parse_args(argv)
+    dist = Dist(args.gpus)
+    try:
+        result = run_reference(args, dist) if args.impl == "reference" else run_ours(args, dist)
+        if result is not None:
+            print(json.dumps(result), flush=True)
+    finally:
+        dist.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

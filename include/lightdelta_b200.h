@@ -1,0 +1,152 @@
+/*
+ * lightdelta_b200.h -- C ABI of the B200 (sm_100a) Gated DeltaNet decode hot path.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes; no
+ * framework types cross this boundary.  All entry points:
+ *   - allocate nothing and never synchronise the host;
+ *   - enqueue their kernels on `stream` (a cudaStream_t passed as void*; NULL is
+ *     the legacy default stream), so a caller may capture them in a CUDA graph;
+ *   - validate their arguments on the host first and return LD_ERR_INVALID with a
+ *     message (ld_last_error) before touching the GPU when a precondition fails;
+ *   - return LD_ERR_CUDA if the launch itself fails.
+ * Data errors (a null or out-of-range slot, an accepted count outside the window)
+ * never fault: the affected request is skipped as described per entry point, and
+ * out-of-range slots additionally raise a bit in the device fault word
+ * (ld_fault_flags).
+ *
+ * Geometry: key/value head dimension K = V = 128.  The state of one
+ * (slot, value head) is a dense fp32 [V, K] matrix (row v, column k), 64 KiB.
+ * A state slot is [HV, V, K]; slots sit `slot_stride` floats apart.
+ */
+#ifndef LIGHTDELTA_B200_H_
+#define LIGHTDELTA_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Return codes. */
+#define LD_OK 0
+#define LD_ERR_INVALID 1 /* a host-checked precondition failed; nothing was launched */
+#define LD_ERR_CUDA 2    /* the CUDA runtime reported an error */
+
+/* Element types of the dtype-polymorphic parameters (dt_bias, norm weight). */
+#define LD_DTYPE_F32 0
+#define LD_DTYPE_BF16 1
+
+/* Bits of the device fault word (ld_fault_flags). */
+#define LD_FAULT_DECODE_SLOT_RANGE 0x1u   /* decode: a slot index >= n_slots */
+#define LD_FAULT_DECODE_TOKENS 0x2u       /* decode: cu[r+1]-cu[r] > width, or cu outside [0, n_tokens] */
+#define LD_FAULT_GATHER_SLOT_RANGE 0x4u   /* gather_state: a slot index >= n_pool_slots */
+#define LD_FAULT_SCATTER_SLOT_RANGE 0x8u  /* scatter_state: a slot index >= n_pool_slots */
+#define LD_FAULT_COPY_SLOT_RANGE 0x10u    /* copy_slots: a slot index >= n_pool_slots */
+
+/* Head dimension handled by every kernel (K = V). */
+#define LD_HEAD_DIM 128
+/* Largest number of tokens per request (MTP verify window), csrc/register.cpp:5-7 schema
+ * limit enforced at csrc/gdn_decode.cu:394-395. */
+#define LD_MAX_WIDTH 4
+
+/* Message of the last LD_ERR_* returned on the calling thread ("" if none). */
+const char* ld_last_error(void);
+
+/* Library version string. */
+const char* ld_version(void);
+
+/*
+ * Fused GDN decode / MTP verify.
+ * Replaces lightdelta::decode (csrc/gdn_decode.cu:360-420, declared at
+ * include/lightdelta/ops.h:5-10, schema csrc/register.cpp:5-7).
+ *
+ * Requests r in [0, n_requests) own tokens cu[r] .. cu[r+1]-1 and a row of `width`
+ * (1..4) int32 state slots indices[r*width + t].  For each (request, value head h):
+ *   source slot  = indices[r*width + accepted[r]-1]   (accepted[r] in 1..width);
+ *   S            = state[source, h]                    (fp32 [128,128]);
+ *   for each token t:  S <- exp(g_t) S;  S <- S + beta_t (v_t - S k_t) k_t^T;
+ *                      o_t = bf16(S q_t);  state[indices[r*width+t], h] <- S if that slot > 0;
+ *   out[token, h, :] = bf16( o_t * rsqrt(mean(o_t^2)+eps) * weight * silu(gate[token,h,:]) ).
+ * q and k are L2-normalised per head in fp32 (q additionally scaled by 128^-1/2);
+ * g = -exp(a_log[h]) * softplus(a + dt_bias[h]); beta = sigmoid(b).
+ * A request with no tokens writes nothing.  A request whose source slot is <= 0,
+ * whose accepted count lies outside 1..width, whose token count exceeds width or whose
+ * source slot is >= n_slots gets zero outputs and no state writes.
+ * Destination slots <= 0 (and >= n_slots) are not written; slot 0 is therefore never
+ * modified.
+ *
+ * qkv      bf16 rows [n_tokens, (2*H+HV)*128] = [q (H*128) | k (H*128) | v (HV*128)], row stride qkv_row_stride
+ * a, b     bf16 [n_tokens, HV], row strides a_row_stride / b_row_stride, unit inner stride
+ * a_log    fp32 [HV];  dt_bias [HV] of dt_bias_dtype;  weight [128] of weight_dtype
+ * indices  int32 [n_requests, width] contiguous;  cu int32 [n_requests+1];  accepted int32 [n_requests]
+ * state    fp32 [n_slots, HV, 128, 128], inner three dims dense, slot stride `slot_stride` floats
+ * gate     bf16 [n_tokens, HV, 128], head stride 128, row stride gate_row_stride
+ * out      bf16 [n_tokens, HV, 128] contiguous
+ */
+int ld_decode(const void* qkv, int64_t qkv_row_stride,
+              const void* a, int64_t a_row_stride,
+              const void* b, int64_t b_row_stride,
+              const float* a_log,
+              const void* dt_bias, int dt_bias_dtype,
+              const int32_t* indices, int64_t n_requests, int64_t width,
+              const int32_t* cu, const int32_t* accepted,
+              float* state, int64_t n_slots, int64_t slot_stride,
+              const void* gate, int64_t gate_row_stride,
+              const void* weight, int weight_dtype,
+              void* out, int64_t n_tokens,
+              int64_t num_k_heads, int64_t num_v_heads,
+              float eps, void* stream);
+
+/*
+ * Slot-indexed gather of whole state slots into a packed buffer.
+ * Replaces lightdelta::gather_state (csrc/state_io.cu:44-58, include/lightdelta/ops.h:11-12,
+ * schema csrc/register.cpp:8).
+ *   out[i] = pool[slots[i*slots_stride]]   if that slot > 0 and valid[i] (and < n_pool_slots)
+ *   out[i] = 0                             otherwise.
+ * pool fp32, slot i at pool + slot*pool_slot_stride, `slot_elems` dense floats per slot;
+ * out fp32 with row stride out_row_stride; valid: n bytes (C bool).
+ */
+int ld_gather_state(const float* pool, int64_t n_pool_slots, int64_t pool_slot_stride,
+                    const int32_t* slots, int64_t slots_stride,
+                    const uint8_t* valid, int64_t n,
+                    float* out, int64_t out_row_stride,
+                    int64_t slot_elems, void* stream);
+
+/*
+ * Slot-indexed scatter of a packed buffer into the pool.
+ * Replaces lightdelta::scatter_state (csrc/state_io.cu:60-69, include/lightdelta/ops.h:13,
+ * schema csrc/register.cpp:9).
+ *   pool[slots[i*slots_stride]] = packed[i]   for every i whose slot is > 0 (and < n_pool_slots).
+ * Rows whose slot is <= 0 are skipped, so slot 0 is never written.  Two rows naming the
+ * same slot race (as in the reference).
+ */
+int ld_scatter_state(const float* packed, int64_t packed_row_stride,
+                     const int32_t* slots, int64_t slots_stride, int64_t n,
+                     float* pool, int64_t n_pool_slots, int64_t pool_slot_stride,
+                     int64_t slot_elems, void* stream);
+
+/*
+ * Pool-to-pool slot copy: the explicit form of committing an accepted MTP step.
+ * Extension with no single counterpart in the reference: it performs in one pass what
+ * python/lightdelta/backend.py:87-91 (index_copy_ commit of live step states) does for a
+ * state that already sits in the pool, i.e. gather_state followed by scatter_state.
+ *   pool[dst[i]] = pool[src[i]]   for every i with src[i] > 0, dst[i] > 0 and src[i] != dst[i].
+ * src/dst are int32 vectors with strides src_stride/dst_stride.  A slot named both as a
+ * source and as a destination of different rows races.
+ */
+int ld_copy_slots(float* pool, int64_t n_pool_slots, int64_t pool_slot_stride,
+                  const int32_t* src, int64_t src_stride,
+                  const int32_t* dst, int64_t dst_stride, int64_t n,
+                  int64_t slot_elems, void* stream);
+
+/*
+ * Reads (and, if clear != 0, resets) the device fault word of the current device into *flags.
+ * This call synchronises the device; it is a diagnostic, not part of the hot path.
+ */
+int ld_fault_flags(uint32_t* flags, int clear);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LIGHTDELTA_B200_H_ */

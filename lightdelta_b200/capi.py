@@ -1,0 +1,148 @@
+"""ctypes binding of the C ABI in include/lightdelta_b200.h (liblightdelta_b200.so).
+
+``lib()`` returns the raw CDLL with argument types set; the tensor helpers below call the
+entry points with torch CUDA tensors (pointers, strides and the current stream), mirroring
+the argument meaning of torch.ops.lightdelta.* without going through the dispatcher.
+There is no CPU fallback: if the library is missing, loading raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "liblightdelta_b200.so"
+
+LD_OK = 0
+LD_ERR_INVALID = 1
+LD_ERR_CUDA = 2
+LD_DTYPE_F32 = 0
+LD_DTYPE_BF16 = 1
+LD_FAULT_DECODE_SLOT_RANGE = 0x1
+LD_FAULT_DECODE_TOKENS = 0x2
+LD_FAULT_GATHER_SLOT_RANGE = 0x4
+LD_FAULT_SCATTER_SLOT_RANGE = 0x8
+LD_FAULT_COPY_SLOT_RANGE = 0x10
+HEAD_DIM = 128
+MAX_WIDTH = 4
+
+_lib: ctypes.CDLL | None = None
+
+
+class LightDeltaError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(message)
+        self.code = code
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise ImportError(
+            f"{LIB_PATH} is missing; build it with `python -m lightdelta_b200.build` "
+            "(lightdelta_b200 has no CPU fallback)"
+        )
+    handle = ctypes.CDLL(str(LIB_PATH))
+    p, i64, i32, f32, u32p = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.POINTER(ctypes.c_uint32)
+    handle.ld_last_error.argtypes = []
+    handle.ld_last_error.restype = ctypes.c_char_p
+    handle.ld_version.argtypes = []
+    handle.ld_version.restype = ctypes.c_char_p
+    handle.ld_decode.argtypes = [
+        p, i64, p, i64, p, i64, p, p, i32, p, i64, i64, p, p, p, i64, i64, p, i64, p, i32, p, i64, i64, i64, f32, p,
+    ]
+    handle.ld_decode.restype = i32
+    handle.ld_gather_state.argtypes = [p, i64, i64, p, i64, p, i64, p, i64, i64, p]
+    handle.ld_gather_state.restype = i32
+    handle.ld_scatter_state.argtypes = [p, i64, p, i64, i64, p, i64, i64, i64, p]
+    handle.ld_scatter_state.restype = i32
+    handle.ld_copy_slots.argtypes = [p, i64, i64, p, i64, p, i64, i64, i64, p]
+    handle.ld_copy_slots.restype = i32
+    handle.ld_fault_flags.argtypes = [u32p, i32]
+    handle.ld_fault_flags.restype = i32
+    _lib = handle
+    return handle
+
+
+def last_error() -> str:
+    return lib().ld_last_error().decode()
+
+
+def version() -> str:
+    return lib().ld_version().decode()
+
+
+def check(rc: int) -> None:
+    if rc != LD_OK:
+        raise LightDeltaError(rc, last_error())
+
+
+def fault_flags(clear: bool = True) -> int:
+    """Device fault word of the current device (synchronises); see LD_FAULT_* constants."""
+    value = ctypes.c_uint32(0)
+    check(lib().ld_fault_flags(ctypes.byref(value), int(clear)))
+    return value.value
+
+
+# ---------------------------------------------------------------------------------------------
+# torch-tensor helpers (C-ABI path)
+# ---------------------------------------------------------------------------------------------
+def _stream(tensor, stream) -> int:
+    import torch
+
+    if stream is None:
+        stream = torch.cuda.current_stream(tensor.device)
+    return stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
+
+
+def _dtype_code(tensor) -> int:
+    import torch
+
+    if tensor.dtype == torch.bfloat16:
+        return LD_DTYPE_BF16
+    if tensor.dtype == torch.float32:
+        return LD_DTYPE_F32
+    raise TypeError(f"unsupported dtype {tensor.dtype}")
+
+
+def decode(qkv, a, b, a_log, dt_bias, indices, cu, accepted, state, gate, weight, out, eps=1e-6, stream=None):
+    """ld_decode on torch tensors laid out as torch.ops.lightdelta.decode expects."""
+    hv = state.shape[1]
+    h = (qkv.shape[1] // HEAD_DIM - hv) // 2
+    check(lib().ld_decode(
+        qkv.data_ptr(), qkv.stride(0), a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), a_log.data_ptr(),
+        dt_bias.data_ptr(), _dtype_code(dt_bias), indices.data_ptr(), indices.shape[0], indices.shape[1],
+        cu.data_ptr(), accepted.data_ptr(), state.data_ptr(), state.shape[0], state.stride(0), gate.data_ptr(),
+        gate.stride(0), weight.data_ptr(), _dtype_code(weight), out.data_ptr(), qkv.shape[0], h, hv, float(eps),
+        _stream(qkv, stream),
+    ))
+
+
+def _slot_elems(pool) -> int:
+    n = 1
+    for d in pool.shape[1:]:
+        n *= d
+    return n
+
+
+def gather_state(pool, slots, valid, out, stream=None):
+    check(lib().ld_gather_state(
+        pool.data_ptr(), pool.shape[0], pool.stride(0), slots.data_ptr(), slots.stride(0), valid.data_ptr(),
+        slots.numel(), out.data_ptr(), out.stride(0), _slot_elems(pool), _stream(pool, stream),
+    ))
+
+
+def scatter_state(packed, slots, pool, stream=None):
+    check(lib().ld_scatter_state(
+        packed.data_ptr(), packed.stride(0), slots.data_ptr(), slots.stride(0), slots.numel(), pool.data_ptr(),
+        pool.shape[0], pool.stride(0), _slot_elems(pool), _stream(pool, stream),
+    ))
+
+
+def copy_slots(pool, src, dst, stream=None):
+    check(lib().ld_copy_slots(
+        pool.data_ptr(), pool.shape[0], pool.stride(0), src.data_ptr(), src.stride(0), dst.data_ptr(),
+        dst.stride(0), src.numel(), _slot_elems(pool), _stream(pool, stream),
+    ))

@@ -1,0 +1,141 @@
+"""Seeded synthetic workloads with the shapes and distributions of the BASELINE configs.
+
+No public dataset exists for this path; these builders restate the configurations:
+  config 1  decode, B=1, T=1                           (CPU-runnable reference case)
+  config 2  indexed decode, B=256, T=1, pool of 1024 fp32 slots [32,128,128]
+  config 3  MTP verify, B=64, T=4, accepted ~ U{1..4}, distinct slots per (request, step)
+  config 4  state-pool copy, pools of 2048 slots, gather 512 slots then scatter to a permutation
+  config 5  stacked decode over 48 layers (T=4 verify), state sharded by sequence slot
+Geometry: H=16 key heads, HV=32 value heads (ratio 2), K=V=128.  q, k, v ~ N(0,1) bf16; a_log =
+dt_bias = 0 so g = -softplus(a) with a ~ N(0,1); b ~ N(0,1) (beta = sigmoid(b)); gate 0.2*N(0,1);
+norm weight N(0,1) bf16; state fp32 N(0, 0.02^2).  qkv and gate are slices of one wider
+projection buffer and a, b slices of another, as vLLM lays them out (reference
+tests/conftest.py:14-28).  Slot 0 is the reserved null slot and is never selected.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+HEAD_DIM = 128
+SLOT_HEAD_BYTES = HEAD_DIM * HEAD_DIM * 4
+
+
+@dataclass
+class DecodeCase:
+    """Arguments of one lightdelta::decode call plus bookkeeping for byte accounting."""
+
+    qkv: torch.Tensor
+    a: torch.Tensor
+    b: torch.Tensor
+    a_log: torch.Tensor
+    dt_bias: torch.Tensor
+    slots: torch.Tensor
+    cu: torch.Tensor
+    accepted: torch.Tensor
+    pool: torch.Tensor
+    gate: torch.Tensor
+    weight: torch.Tensor
+    out: torch.Tensor
+    eps: float = 1e-6
+    num_k_heads: int = 16
+    extra: dict = field(default_factory=dict)
+
+    def kwargs(self) -> dict:
+        return dict(qkv=self.qkv, a=self.a, b=self.b, a_log=self.a_log, dt_bias=self.dt_bias, slots=self.slots,
+                    cu=self.cu, accepted=self.accepted, pool=self.pool, gate=self.gate, weight=self.weight,
+                    out=self.out, eps=self.eps)
+
+    def op_args(self) -> tuple:
+        """Positional arguments of torch.ops.lightdelta.decode."""
+        return (self.qkv, self.a, self.b, self.a_log, self.dt_bias, self.slots, self.cu, self.accepted, self.pool,
+                self.gate, self.weight, self.out, self.eps)
+
+    @property
+    def num_v_heads(self) -> int:
+        return self.pool.shape[1]
+
+    @property
+    def tokens(self) -> int:
+        return self.qkv.shape[0]
+
+
+def activation_bytes_per_token(num_k_heads: int, num_v_heads: int) -> int:
+    """q + k + v + gate + out (bf16) and a, b (bf16) for one token."""
+    qkv = (2 * num_k_heads + num_v_heads) * HEAD_DIM * 2
+    gate = out = num_v_heads * HEAD_DIM * 2
+    ab = 2 * num_v_heads * 2
+    return qkv + gate + out + ab
+
+
+def decode_algorithmic_bytes(requests: int, width: int, tokens: int, num_k_heads: int, num_v_heads: int) -> int:
+    """State read once per request, written once per step, plus activations."""
+    slot = num_v_heads * SLOT_HEAD_BYTES
+    return requests * (1 + width) * slot + tokens * activation_bytes_per_token(num_k_heads, num_v_heads)
+
+
+def make_decode_case(batch: int, width: int, pool_slots: int, *, device, seed: int, num_k_heads: int = 16,
+                     num_v_heads: int = 32, accepted: str = "ones", state_scale: float = 0.02,
+                     pool: torch.Tensor | None = None) -> DecodeCase:
+    """A decode (width 1) or MTP verify (width > 1) case with distinct random slots in 1..pool_slots-1.
+
+    accepted: "ones" (all 1) or "uniform" (U{1..width}).  If `pool` is given it is used as is
+    (layer pools shared across cases) and must have `pool_slots` slots.
+    """
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    n = batch * width
+    hv, h = num_v_heads, num_k_heads
+    qkv_width = (2 * h + hv) * HEAD_DIM
+    if batch * width > pool_slots - 1:
+        raise ValueError("pool too small for distinct slots")
+    proj = torch.randn(n, qkv_width + hv * HEAD_DIM, device=device, generator=gen, dtype=torch.float32)
+    proj[:, qkv_width:] *= 0.2
+    proj = proj.to(torch.bfloat16)
+    ba = torch.randn(n, 2 * hv, device=device, generator=gen).to(torch.bfloat16)
+    perm = torch.randperm(pool_slots - 1, device=device, generator=gen)[: batch * width] + 1
+    slots = perm.to(torch.int32).view(batch, width).contiguous()
+    if accepted == "ones":
+        acc = torch.ones(batch, device=device, dtype=torch.int32)
+    elif accepted == "uniform":
+        acc = torch.randint(1, width + 1, (batch,), device=device, generator=gen, dtype=torch.int32)
+    else:
+        raise ValueError(accepted)
+    if pool is None:
+        pool = torch.empty(pool_slots, hv, HEAD_DIM, HEAD_DIM, device=device, dtype=torch.float32)
+        pool.normal_(0.0, state_scale, generator=gen)
+    weight = torch.randn(HEAD_DIM, device=device, generator=gen).to(torch.bfloat16)
+    return DecodeCase(
+        qkv=proj[:, :qkv_width],
+        a=ba[:, hv:],
+        b=ba[:, :hv],
+        a_log=torch.zeros(hv, device=device, dtype=torch.float32),
+        dt_bias=torch.zeros(hv, device=device, dtype=torch.float32),
+        slots=slots,
+        cu=torch.arange(0, n + 1, width, device=device, dtype=torch.int32),
+        accepted=acc,
+        pool=pool,
+        gate=proj[:, qkv_width:].view(n, hv, HEAD_DIM),
+        weight=weight,
+        out=torch.empty(n, hv, HEAD_DIM, device=device, dtype=torch.bfloat16),
+        num_k_heads=h,
+    )
+
+
+def config2(device, seed: int = 2, pool: torch.Tensor | None = None) -> DecodeCase:
+    return make_decode_case(256, 1, 1024, device=device, seed=seed, pool=pool)
+
+
+def config3(device, seed: int = 3, pool_slots: int = 1 + 256, pool: torch.Tensor | None = None) -> DecodeCase:
+    return make_decode_case(64, 4, pool_slots, device=device, seed=seed, accepted="uniform", pool=pool)
+
+
+def config4_indices(device, seed: int = 4, pool_slots: int = 2048, count: int = 512):
+    """Gather 512 distinct slots of 1..2047, scatter them to a permutation of another distinct set."""
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    gather = (torch.randperm(pool_slots - 1, device=device, generator=gen)[:count] + 1).to(torch.int32)
+    scatter = (torch.randperm(pool_slots - 1, device=device, generator=gen)[:count] + 1).to(torch.int32)
+    return gather, scatter

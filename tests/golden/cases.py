@@ -1,0 +1,130 @@
+"""Case definitions shared by tests/golden/make_golden.py and the tests that read the fixtures.
+
+Every input is regenerated from its seed with tests/golden/detrand.py, so the fixtures hold
+only results.  Distributions follow the reference's test fixture (tests/conftest.py:5-33:
+qkvz*0.2, ba ~ N(0,1), pool*0.1, bf16 dt_bias and norm weight) and, for the HV=32 cases, the
+BASELINE configs (q, k, v ~ N(0,1); a_log = dt_bias = 0 so g = -softplus(a); state ~ N(0, 0.02^2);
+gate 0.2*N(0,1)).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from . import detrand
+
+D = 128
+
+POST_CONV_CASES = [
+    # The reference's own odd-shape case (tests/test_gdn.py:7-44): fp32 io, lengths [4,2,0].
+    dict(name="post_conv_small", seed=7, B=3, T=4, Hk=2, Hv=6, K=5, V=7, io_bf16=False, checkpoints=True,
+         lengths=[4, 2, 0], eps=1e-6, samples=None, baseline=False),
+    # B=1, T=1, H=16, HV=32, K=V=128, bf16 activations.
+    dict(name="post_conv_hv32_t1", seed=11, B=1, T=1, Hk=16, Hv=32, K=D, V=D, io_bf16=True, checkpoints=False,
+         lengths=[1], eps=1e-6, samples=32768, baseline=True),
+    # MTP-shaped multi-step run with per-step checkpoints and one short request.
+    dict(name="post_conv_hv32_t4", seed=13, B=2, T=4, Hk=16, Hv=32, K=D, V=D, io_bf16=True, checkpoints=True,
+         lengths=[4, 2], eps=1e-6, samples=65536, baseline=True),
+    # HV=48 geometry with non-zero a_log / dt_bias and a masked (length 0) request.
+    dict(name="post_conv_hv48_t3", seed=17, B=2, T=3, Hk=16, Hv=48, K=D, V=D, io_bf16=True, checkpoints=False,
+         lengths=[3, 0], eps=1e-5, samples=32768, baseline=False),
+]
+
+BACKEND_CASES = [
+    # tests/test_gdn.py:58-75: mixed accepted counts, one padding request (slots[-1] = 0).
+    *[dict(name=f"backend_hv48_w{w}", seed=42, batch=4, width=w, mutation="mixed", samples_per_slot=256)
+      for w in (1, 2, 3, 4)],
+    # tests/test_gdn.py:105-122: ragged tokens, invalid request, discarded candidate slot.
+    dict(name="backend_hv48_ragged", seed=42, batch=4, width=4, mutation="ragged", samples_per_slot=256),
+    # tests/test_gdn.py:78-102: flipped slot rows and accepted = 2.
+    dict(name="backend_hv48_flipped", seed=42, batch=2, width=3, mutation="flipped", samples_per_slot=256),
+]
+
+
+def spec_by_name(name: str) -> dict:
+    for spec in POST_CONV_CASES + BACKEND_CASES:
+        if spec["name"] == name:
+            return spec
+    raise KeyError(name)
+
+
+def sample_positions(seed: int, size: int, samples: int | None) -> np.ndarray:
+    if samples is None or samples >= size:
+        return np.arange(size, dtype=np.int64)
+    return np.unique(detrand.integers(seed, samples, size))
+
+
+def per_slot_positions(seed: int, shape, per_slot: int) -> np.ndarray:
+    slots = shape[0]
+    elems = int(np.prod(shape[1:]))
+    rows = [s * elems + np.unique(detrand.integers(seed + s, per_slot, elems)) for s in range(slots)]
+    return np.concatenate(rows).astype(np.int64)
+
+
+def post_conv_inputs(spec: dict) -> dict:
+    """fp32 arrays (already rounded to bf16 where the case uses bf16 activations)."""
+    B, T, Hk, Hv, K, V = (spec[k] for k in ("B", "T", "Hk", "Hv", "K", "V"))
+    s = spec["seed"] * 16
+
+    def act(seed, shape, scale=1.0):
+        values = detrand.normal(seed, shape, scale)
+        return detrand.bf16_values(detrand.bf16_bits(values)) if spec["io_bf16"] else values
+
+    arrays = dict(
+        q=act(s + 1, (B, T, Hk, K)),
+        k=act(s + 2, (B, T, Hk, K)),
+        v=act(s + 3, (B, T, Hv, V)),
+        a=act(s + 4, (B, T, Hv)),
+        b=act(s + 5, (B, T, Hv)),
+        gate=act(s + 8, (B, T, Hv, V), 0.2 if spec["baseline"] else 1.0),
+    )
+    if spec["baseline"]:
+        arrays["a_log"] = np.zeros(Hv, np.float32)
+        arrays["dt_bias"] = np.zeros(Hv, np.float32)
+        arrays["initial_state"] = detrand.normal(s + 9, (B, Hv, V, K), 0.02)
+    else:
+        arrays["a_log"] = detrand.normal(s + 6, (Hv,))
+        arrays["dt_bias"] = detrand.normal(s + 7, (Hv,))
+        arrays["initial_state"] = detrand.normal(s + 9, (B, Hv, V, K))
+    arrays["norm_weight"] = detrand.normal(s + 10, (V,))
+    arrays["lengths"] = np.asarray(spec["lengths"], np.int64)
+    return arrays
+
+
+def backend_case(spec: dict) -> dict:
+    """Inputs of a GDNBackend call at the reference geometry (H=16, HV=48), as numpy arrays.
+
+    bf16 tensors are uint16 bit arrays: qkvz [n,16384] (qkv = [:, :10240], gate = [:, 10240:]),
+    ba [n,96] (b = [:, :48], a = [:, 48:]) exactly as the reference fixture slices them.
+    """
+    batch, width = spec["batch"], spec["width"]
+    n = batch * width
+    hv, h = 48, 16
+    qkv_width = (2 * h + hv) * D
+    s = spec["seed"] * 10
+    arrays = dict(
+        qkvz_bits=detrand.bf16_bits(detrand.normal(s + 1, (n, qkv_width + hv * D), 0.2)),
+        ba_bits=detrand.bf16_bits(detrand.normal(s + 2, (n, 2 * hv))),
+        a_log=detrand.normal(s + 3, (hv,)),
+        dt_bias_bits=detrand.bf16_bits(detrand.normal(s + 4, (hv,))),
+        pool=detrand.normal(s + 5, (n + 2, hv, D, D), 0.1),
+        weight_bits=detrand.bf16_bits(detrand.normal(s + 6, (D,))),
+        slots=np.arange(1, n + 1, dtype=np.int32).reshape(batch, width),
+        cu=np.arange(0, n + 1, width, dtype=np.int32),
+        accepted=np.ones(batch, np.int32),
+    )
+    rows = n
+    if spec["mutation"] == "mixed":
+        arrays["accepted"][:] = np.arange(batch) % width + 1
+        arrays["slots"][-1] = 0
+    elif spec["mutation"] == "ragged":
+        arrays["cu"] = np.array([0, 4, 7, 8, 8], np.int32)
+        arrays["accepted"][0] = 0
+        arrays["slots"][1, 2] = 0
+        rows = 8
+    elif spec["mutation"] == "flipped":
+        arrays["slots"] = np.ascontiguousarray(arrays["slots"][::-1])
+        arrays["accepted"][:] = 2
+    else:
+        raise ValueError(spec["mutation"])
+    return dict(arrays=arrays, rows=rows, hv=hv, h=h, qkv_width=qkv_width)

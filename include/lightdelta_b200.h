@@ -42,6 +42,7 @@ extern "C" {
 #define LD_FAULT_GATHER_SLOT_RANGE 0x4u   /* gather_state: a slot index >= n_pool_slots */
 #define LD_FAULT_SCATTER_SLOT_RANGE 0x8u  /* scatter_state: a slot index >= n_pool_slots */
 #define LD_FAULT_COPY_SLOT_RANGE 0x10u    /* copy_slots: a slot index >= n_pool_slots */
+#define LD_FAULT_WAIT_TIMEOUT 0x20u       /* a bounded in-kernel wait expired; that launch's results are incomplete */
 
 /* Head dimension handled by every kernel (K = V). */
 #define LD_HEAD_DIM 128
@@ -138,6 +139,22 @@ int ld_copy_slots(float* pool, int64_t n_pool_slots, int64_t pool_slot_stride,
                   const int32_t* src, int64_t src_stride,
                   const int32_t* dst, int64_t dst_stride, int64_t n,
                   int64_t slot_elems, void* stream);
+
+/* Decode kernel variants (ld_decode_kernel_override). */
+#define LD_DECODE_KERNEL_AUTO 0          /* library default: STREAM_4ROW for width 1, ROWREG otherwise */
+#define LD_DECODE_KERNEL_ROWREG 1        /* one CTA per (request, head), state loaded into registers */
+#define LD_DECODE_KERNEL_STREAM_4ROW 2   /* persistent TMA-bulk streaming kernel, 8 consumer warps */
+#define LD_DECODE_KERNEL_STREAM_2ROW 3   /* persistent TMA-bulk streaming kernel, 16 consumer warps */
+#define LD_DECODE_KERNEL_TMA_STORE 4     /* persistent kernel with TMA bulk loads and TMA bulk stores */
+
+/*
+ * Process-wide choice of the kernel that ld_decode launches, for tuning and for testing every
+ * variant against the oracle; all variants compute the same results.  Streaming variants need
+ * 16-byte aligned qkv / gate rows and fall back to LD_DECODE_KERNEL_ROWREG otherwise.
+ * Returns the previous setting, or -LD_ERR_INVALID for an unknown variant.
+ * No counterpart in the reference, which has a single kernel (csrc/gdn_decode.cu:130).
+ */
+int ld_decode_kernel_override(int variant);
 
 /*
  * Reads (and, if clear != 0, resets) the device fault word of the current device into *flags.

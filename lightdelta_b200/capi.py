@@ -23,8 +23,10 @@ LD_FAULT_DECODE_TOKENS = 0x2
 LD_FAULT_GATHER_SLOT_RANGE = 0x4
 LD_FAULT_SCATTER_SLOT_RANGE = 0x8
 LD_FAULT_COPY_SLOT_RANGE = 0x10
+LD_FAULT_WAIT_TIMEOUT = 0x20
 HEAD_DIM = 128
 MAX_WIDTH = 4
+DECODE_KERNELS = {"auto": 0, "rowreg": 1, "stream4": 2, "stream2": 3, "tmastore": 4}
 
 _lib: ctypes.CDLL | None = None
 
@@ -62,6 +64,8 @@ def lib() -> ctypes.CDLL:
     handle.ld_copy_slots.restype = i32
     handle.ld_fault_flags.argtypes = [u32p, i32]
     handle.ld_fault_flags.restype = i32
+    handle.ld_decode_kernel_override.argtypes = [i32]
+    handle.ld_decode_kernel_override.restype = i32
     _lib = handle
     return handle
 
@@ -84,6 +88,15 @@ def fault_flags(clear: bool = True) -> int:
     value = ctypes.c_uint32(0)
     check(lib().ld_fault_flags(ctypes.byref(value), int(clear)))
     return value.value
+
+
+def set_decode_kernel(name: str) -> str:
+    """Select the kernel ld_decode launches ("auto", "rowreg", "stream4", "stream2"); returns the
+    previous selection.  All variants compute the same results."""
+    previous = lib().ld_decode_kernel_override(DECODE_KERNELS[name])
+    if previous < 0:
+        raise LightDeltaError(-previous, last_error())
+    return {v: k for k, v in DECODE_KERNELS.items()}[previous]
 
 
 # ---------------------------------------------------------------------------------------------

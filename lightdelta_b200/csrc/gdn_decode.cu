@@ -4,21 +4,38 @@
 // :360-420 launcher), generalised to any num_k_heads / num_v_heads with K = V = 128.
 // Mathematics: python/lightdelta/reference/gdn.py:70-128 (post_conv_gdn).
 //
-// Design (B200): the op is a read-modify-write stream over fp32 state slots, so it is
-// HBM bound (about 1 flop per byte at one token).  One CTA owns one (request, value head)
-// pair and keeps the whole 128x128 fp32 state in registers: 256 threads, each holding
-// 4 rows x 16 columns (64 floats).  Eight lanes share a row; lane j of a row group owns
-// columns {32c + 4j .. 32c + 4j + 3 : c = 0..3}, so every warp-wide 128-bit load or store
-// touches four fully used 128-byte lines.  All 16 loads of a thread are issued before the
-// activations are prepared, giving 64 KiB in flight per CTA (128 KiB per SM at two CTAs).
-// Row dot products (S k and S q) are reduced with three xor-shuffles inside the 8-lane
-// group.  Each step's state goes straight from registers to its destination slot.
-// Tensor cores are not used: per token the work is a rank-1 update plus two GEMVs.
+// The op is a read-modify-write stream over fp32 state slots: about one flop per byte at one
+// token, so HBM bandwidth bounds it and tensor cores have nothing to do (per token the work is
+// a rank-1 update plus two GEMVs per (sequence, value head)).
+//
+// Work unit ("item"): one (request, value head) pair, i.e. one 128x128 fp32 state (64 KiB)
+// read once and written once per token step.
+//
+// Register tile shared by both kernels: 256 compute threads hold the whole state, 4 rows x 16
+// columns each.  Eight lanes share a row; lane j of a row group owns columns
+// {32c + 4j .. 32c + 4j + 3 : c = 0..3}, so each warp-wide 128-bit access touches four fully
+// used 128-byte lines, and the row dot products S k and S q reduce with three xor-shuffles.
+//
+// gdn_decode_stream_kernel (default): persistent, one CTA per SM.  A producer warp streams the
+// states of the CTA's items into a 3-deep shared-memory ring with TMA bulk copies
+// (cp.async.bulk, completion on an mbarrier) together with the items' q/k/v/gate rows, while
+// 8 consumer warps run the recurrence on the register tile and store each step's state
+// straight from registers.  Up to three 64 KiB states per SM are in flight at all times, so
+// HBM never waits for a CTA's compute or store phase.  Every mbarrier wait is bounded
+// (LD_FAULT_WAIT_TIMEOUT).  No cluster and no multicast: each CTA reads only its own items
+// from this GPU's memory.
+//
+// gdn_decode_rowreg_kernel (fallback): one CTA per item, loading the state straight into
+// registers with 128-bit loads.  Used when the activation rows are not 16-byte aligned (TMA
+// bulk copies need 16-byte aligned sources).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cmath>
 #include <cstdint>
+#include <algorithm>
+#include <atomic>
+#include <mutex>
 
 #include "internal.h"
 #include "lightdelta_b200.h"
@@ -28,11 +45,17 @@ namespace {
 
 constexpr int kDim = LD_HEAD_DIM;                      // K = V = 128
 constexpr int kHeadElems = kDim * kDim;                // floats per (slot, value head)
-constexpr int kThreads = 256;
+constexpr int kHeadBytes = kHeadElems * 4;             // 65,536
+constexpr int kRowBytes = kDim * 2;                    // one bf16 head row: 256 B
 constexpr int kLanesPerRow = 8;                        // lanes sharing one state row
-constexpr int kRowGroups = kThreads / kLanesPerRow;    // 32 rows in flight per pass
-constexpr int kRowsPerThread = kDim / kRowGroups;      // 4
 constexpr int kVecPerRow = kDim / (4 * kLanesPerRow);  // float4 per lane per row: 4
+
+// Register tile with kRows rows per thread: kDim / kRows row groups of 8 lanes.
+template <int kRows>
+struct Tile {
+  static constexpr int kRowGroups = kDim / kRows;             // rows covered per pass
+  static constexpr int kThreads = kRowGroups * kLanesPerRow;  // 256 (4 rows) or 512 (2 rows)
+};
 constexpr int kMaxTokens = LD_MAX_WIDTH;
 
 __device__ unsigned int g_decode_faults;
@@ -57,6 +80,7 @@ struct DecodeArgs {
   const void* weight;
   __nv_bfloat16* out;
   int64_t n_tokens;
+  int64_t total_items;
   int width;
   int num_k_heads;
   int num_v_heads;
@@ -67,6 +91,9 @@ struct DecodeArgs {
   float eps;
 };
 
+// ------------------------------------------------------------------------------------------
+// scalar helpers
+// ------------------------------------------------------------------------------------------
 __device__ __forceinline__ float bf16_lo(uint32_t x) { return __uint_as_float(x << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t x) { return __uint_as_float(x & 0xffff0000u); }
 
@@ -122,8 +149,117 @@ __device__ __forceinline__ float load_param(const void* p, int index, int is_bf1
 // softplus with torch's default threshold 20 (reference gdn.py:102, gdn_decode.cu:96-98).
 __device__ __forceinline__ float softplus(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
 
+// decay = exp(-exp(A_log) * softplus(a + dt_bias)), beta = sigmoid(b): gdn.py:102-103.
+__device__ __forceinline__ void token_gates(const DecodeArgs& p, int64_t token, int head, float& decay,
+                                            float& beta) {
+  const float a_val = __bfloat162float(p.a[token * p.a_row + head]);
+  const float b_val = __bfloat162float(p.b[token * p.b_row + head]);
+  const float dt = load_param(p.dt_bias, head, p.dt_bias_bf16);
+  decay = expf(-expf(p.a_log[head]) * softplus(a_val + dt));
+  beta = 1.0f / (1.0f + expf(-b_val));
+}
+
+// One delta-rule step on the register tile (gdn.py:111-114), then o = S q for the tile's rows
+// (gdn.py:115), reduced over the row group.  kv / qv are this lane's normalised k and q columns.
+template <int kRows>
+__device__ __forceinline__ void tile_step(float4 (&s)[kRows][kVecPerRow], const float4 (&kv)[kVecPerRow],
+                                          const float4 (&qv)[kVecPerRow], const float (&vrow)[kRows],
+                                          float decay, float beta, float (&o)[kRows]) {
+  float pred[kRows];
+#pragma unroll
+  for (int i = 0; i < kRows; ++i) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int c = 0; c < kVecPerRow; ++c) {
+      s[i][c].x *= decay;
+      s[i][c].y *= decay;
+      s[i][c].z *= decay;
+      s[i][c].w *= decay;
+      acc = fmaf(s[i][c].x, kv[c].x, acc);
+      acc = fmaf(s[i][c].y, kv[c].y, acc);
+      acc = fmaf(s[i][c].z, kv[c].z, acc);
+      acc = fmaf(s[i][c].w, kv[c].w, acc);
+    }
+    pred[i] = acc;
+  }
+#pragma unroll
+  for (int i = 0; i < kRows; ++i) pred[i] = row_sum(pred[i]);
+#pragma unroll
+  for (int i = 0; i < kRows; ++i) {
+    const float delta = (vrow[i] - pred[i]) * beta;
+#pragma unroll
+    for (int c = 0; c < kVecPerRow; ++c) {
+      s[i][c].x = fmaf(delta, kv[c].x, s[i][c].x);
+      s[i][c].y = fmaf(delta, kv[c].y, s[i][c].y);
+      s[i][c].z = fmaf(delta, kv[c].z, s[i][c].z);
+      s[i][c].w = fmaf(delta, kv[c].w, s[i][c].w);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kRows; ++i) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int c = 0; c < kVecPerRow; ++c) {
+      acc = fmaf(s[i][c].x, qv[c].x, acc);
+      acc = fmaf(s[i][c].y, qv[c].y, acc);
+      acc = fmaf(s[i][c].z, qv[c].z, acc);
+      acc = fmaf(s[i][c].w, qv[c].w, acc);
+    }
+    o[i] = acc;
+  }
+#pragma unroll
+  for (int i = 0; i < kRows; ++i) o[i] = row_sum(o[i]);
+}
+
+template <int kRows>
+__device__ __forceinline__ void store_tile(float* dst_head, int g, int j, const float4 (&s)[kRows][kVecPerRow]) {
+  float4* ptr = reinterpret_cast<float4*>(dst_head + g * kDim + 4 * j);
+#pragma unroll
+  for (int i = 0; i < kRows; ++i) {
+#pragma unroll
+    for (int c = 0; c < kVecPerRow; ++c) ptr[(i * Tile<kRows>::kRowGroups * kDim + c * 4 * kLanesPerRow) / 4] = s[i][c];
+  }
+}
+
+// Shared-memory or global state of one head -> register tile.
+template <int kRows>
+__device__ __forceinline__ void load_tile(const float* head, int g, int j, float4 (&s)[kRows][kVecPerRow]) {
+  const float4* ptr = reinterpret_cast<const float4*>(head + g * kDim + 4 * j);
+#pragma unroll
+  for (int i = 0; i < kRows; ++i) {
+#pragma unroll
+    for (int c = 0; c < kVecPerRow; ++c) s[i][c] = ptr[(i * Tile<kRows>::kRowGroups * kDim + c * 4 * kLanesPerRow) / 4];
+  }
+}
+
+// Gated RMSNorm of one token's 128 recurrence outputs (already bf16-rounded), gdn.py:117-119:
+// out = bf16(o * rsqrt(mean(o^2) + eps) * w * silu(z)).  One warp, 4 values per lane.
+template <bool kVec>
+__device__ __forceinline__ void gated_rmsnorm_store(const float* o_row, const float (&z)[4], const float (&w)[4],
+                                                    float eps, int lane, __nv_bfloat16* out_row) {
+  float o[4];
+  float sq = 0.0f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    o[e] = o_row[4 * lane + e];
+    sq += o[e] * o[e];
+  }
+  sq = warp_sum(sq);
+  const float rstd = 1.0f / sqrtf(sq / static_cast<float>(kDim) + eps);
+  float y[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float silu = z[e] / (1.0f + expf(-z[e]));
+    y[e] = o[e] * rstd * w[e] * silu;
+  }
+  store4_bf16<kVec>(out_row + 4 * lane, y);
+}
+
+// ==========================================================================================
+// Fallback kernel: one CTA per item, state loaded straight into registers.
+// ==========================================================================================
 template <bool kVecAct>
-__global__ void __launch_bounds__(kThreads, 2) gdn_decode_kernel(const DecodeArgs p) {
+__global__ void __launch_bounds__(Tile<4>::kThreads, 2) gdn_decode_rowreg_kernel(const DecodeArgs p) {
   __shared__ float4 sh_q[kMaxTokens][kDim / 4];
   __shared__ float4 sh_k[kMaxTokens][kDim / 4];
   __shared__ float sh_v[kMaxTokens][kDim];
@@ -133,6 +269,9 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_kernel(const DecodeArg
   __shared__ float sh_beta[kMaxTokens];
   __shared__ int sh_dst[kMaxTokens];
 
+  constexpr int kRows = 4;
+  constexpr int kThreads = Tile<kRows>::kThreads;
+  constexpr int kRowGroups = Tile<kRows>::kRowGroups;
   const int HV = p.num_v_heads;
   const int request = blockIdx.x / HV;
   const int head = blockIdx.x - request * HV;
@@ -164,22 +303,14 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_kernel(const DecodeArg
     return;
   }
 
-  // ---- issue the 64 KiB state read first: 16 x 128-bit loads per thread ----
+  // Issue the 64 KiB state read first: 16 x 128-bit loads per thread.
   const int j = tid & (kLanesPerRow - 1);
   const int g = tid / kLanesPerRow;
-  const int64_t head_offset = static_cast<int64_t>(head) * kHeadElems + g * kDim + 4 * j;
-  const float4* src_ptr =
-      reinterpret_cast<const float4*>(p.state + static_cast<int64_t>(src) * p.slot_stride + head_offset);
-  float4 s[kRowsPerThread][kVecPerRow];
-#pragma unroll
-  for (int i = 0; i < kRowsPerThread; ++i) {
-#pragma unroll
-    for (int c = 0; c < kVecPerRow; ++c) {
-      s[i][c] = src_ptr[(i * kRowGroups * kDim + c * 4 * kLanesPerRow) / 4];
-    }
-  }
+  const int64_t head_offset = static_cast<int64_t>(head) * kHeadElems;
+  float4 s[kRows][kVecPerRow];
+  load_tile<kRows>(p.state + static_cast<int64_t>(src) * p.slot_stride + head_offset, g, j, s);
 
-  // ---- per-token activations: warp t prepares token t ----
+  // Per-token activations: warp t prepares token t.
   if (warp < n) {
     const int t = warp;
     const int64_t token = bos + t;
@@ -202,8 +333,8 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_kernel(const DecodeArg
     // L2 norm in fp32 as gdn.py:98-99; q then scaled by K^-1/2 as gdn.py:101.
     const float q_inv = 1.0f / sqrtf(q_sq + 1e-6f);
     const float k_inv = 1.0f / sqrtf(k_sq + 1e-6f);
-    sh_q[t][lane] = make_float4(q[0] * q_inv * p.q_scale, q[1] * q_inv * p.q_scale,
-                                q[2] * q_inv * p.q_scale, q[3] * q_inv * p.q_scale);
+    sh_q[t][lane] = make_float4(q[0] * q_inv * p.q_scale, q[1] * q_inv * p.q_scale, q[2] * q_inv * p.q_scale,
+                                q[3] * q_inv * p.q_scale);
     sh_k[t][lane] = make_float4(k[0] * k_inv, k[1] * k_inv, k[2] * k_inv, k[3] * k_inv);
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -211,12 +342,7 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_kernel(const DecodeArg
       sh_z[t][4 * lane + e] = z[e];
     }
     if (lane == 0) {
-      // decay = exp(-exp(A_log) * softplus(a + dt_bias)), beta = sigmoid(b): gdn.py:102-103.
-      const float a_val = __bfloat162float(p.a[token * p.a_row + head]);
-      const float b_val = __bfloat162float(p.b[token * p.b_row + head]);
-      const float dt = load_param(p.dt_bias, head, p.dt_bias_bf16);
-      sh_decay[t] = expf(-expf(p.a_log[head]) * softplus(a_val + dt));
-      sh_beta[t] = 1.0f / (1.0f + expf(-b_val));
+      token_gates(p, token, head, sh_decay[t], sh_beta[t]);
       int dst = p.indices[request * W + t];
       if (dst >= p.n_slots) {
         atomicOr(&g_decode_faults, LD_FAULT_DECODE_SLOT_RANGE);
@@ -227,117 +353,752 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_kernel(const DecodeArg
   }
   __syncthreads();
 
-  // ---- recurrence: state stays in registers across the T steps ----
-  const int row0 = g;  // rows owned: g + 32 i
   for (int t = 0; t < n; ++t) {
-    const float decay = sh_decay[t];
-    const float beta = sh_beta[t];
-    float4 kv[kVecPerRow];
+    float4 kv[kVecPerRow], qv[kVecPerRow];
 #pragma unroll
-    for (int c = 0; c < kVecPerRow; ++c) kv[c] = sh_k[t][c * kLanesPerRow + j];
-
-    float pred[kRowsPerThread];
-#pragma unroll
-    for (int i = 0; i < kRowsPerThread; ++i) {
-      float acc_hk = 0.0f;
-#pragma unroll
-      for (int c = 0; c < kVecPerRow; ++c) {
-        s[i][c].x *= decay;
-        s[i][c].y *= decay;
-        s[i][c].z *= decay;
-        s[i][c].w *= decay;
-        acc_hk = fmaf(s[i][c].x, kv[c].x, acc_hk);
-        acc_hk = fmaf(s[i][c].y, kv[c].y, acc_hk);
-        acc_hk = fmaf(s[i][c].z, kv[c].z, acc_hk);
-        acc_hk = fmaf(s[i][c].w, kv[c].w, acc_hk);
-      }
-      pred[i] = acc_hk;
+    for (int c = 0; c < kVecPerRow; ++c) {
+      kv[c] = sh_k[t][c * kLanesPerRow + j];
+      qv[c] = sh_q[t][c * kLanesPerRow + j];
     }
+    float vrow[kRows], o[kRows];
 #pragma unroll
-    for (int i = 0; i < kRowsPerThread; ++i) pred[i] = row_sum(pred[i]);
-
-#pragma unroll
-    for (int i = 0; i < kRowsPerThread; ++i) {
-      const float delta = (sh_v[t][row0 + i * kRowGroups] - pred[i]) * beta;
-#pragma unroll
-      for (int c = 0; c < kVecPerRow; ++c) {
-        s[i][c].x = fmaf(delta, kv[c].x, s[i][c].x);
-        s[i][c].y = fmaf(delta, kv[c].y, s[i][c].y);
-        s[i][c].z = fmaf(delta, kv[c].z, s[i][c].z);
-        s[i][c].w = fmaf(delta, kv[c].w, s[i][c].w);
-      }
-    }
-
-    float4 qv[kVecPerRow];
-#pragma unroll
-    for (int c = 0; c < kVecPerRow; ++c) qv[c] = sh_q[t][c * kLanesPerRow + j];
-    float o[kRowsPerThread];
-#pragma unroll
-    for (int i = 0; i < kRowsPerThread; ++i) {
-      float acc_hq = 0.0f;
-#pragma unroll
-      for (int c = 0; c < kVecPerRow; ++c) {
-        acc_hq = fmaf(s[i][c].x, qv[c].x, acc_hq);
-        acc_hq = fmaf(s[i][c].y, qv[c].y, acc_hq);
-        acc_hq = fmaf(s[i][c].z, qv[c].z, acc_hq);
-        acc_hq = fmaf(s[i][c].w, qv[c].w, acc_hq);
-      }
-      o[i] = acc_hq;
-    }
-#pragma unroll
-    for (int i = 0; i < kRowsPerThread; ++i) o[i] = row_sum(o[i]);
+    for (int i = 0; i < kRows; ++i) vrow[i] = sh_v[t][g + i * kRowGroups];
+    tile_step<kRows>(s, kv, qv, vrow, sh_decay[t], sh_beta[t], o);
     if (j == 0) {
 #pragma unroll
-      for (int i = 0; i < kRowsPerThread; ++i) {
+      for (int i = 0; i < kRows; ++i) {
         // The recurrence output is rounded to bf16 before the norm (gdn.py:116).
-        sh_o[t][row0 + i * kRowGroups] = __bfloat162float(__float2bfloat16_rn(o[i]));
+        sh_o[t][g + i * kRowGroups] = __bfloat162float(__float2bfloat16_rn(o[i]));
       }
     }
-
     const int dst = sh_dst[t];
-    if (dst > 0) {
-      float4* dst_ptr =
-          reinterpret_cast<float4*>(p.state + static_cast<int64_t>(dst) * p.slot_stride + head_offset);
-#pragma unroll
-      for (int i = 0; i < kRowsPerThread; ++i) {
-#pragma unroll
-        for (int c = 0; c < kVecPerRow; ++c) {
-          dst_ptr[(i * kRowGroups * kDim + c * 4 * kLanesPerRow) / 4] = s[i][c];
-        }
-      }
-    }
+    if (dst > 0) store_tile<kRows>(p.state + static_cast<int64_t>(dst) * p.slot_stride + head_offset, g, j, s);
   }
   __syncthreads();
 
-  // ---- gated RMSNorm epilogue: warp t finishes token t (gdn.py:117-119) ----
   if (warp < n) {
     const int t = warp;
-    const int64_t token = bos + t;
-    float o[4];
-    float sq = 0.0f;
+    float z[4], w[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      o[e] = sh_o[t][4 * lane + e];
-      sq += o[e] * o[e];
+      z[e] = sh_z[t][4 * lane + e];
+      w[e] = load_param(p.weight, 4 * lane + e, p.weight_bf16);
     }
-    sq = warp_sum(sq);
-    const float rstd = 1.0f / sqrtf(sq / static_cast<float>(kDim) + p.eps);
-    float y[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int dim = 4 * lane + e;
-      const float z = sh_z[t][dim];
-      const float silu = z / (1.0f + expf(-z));
-      const float w = load_param(p.weight, dim, p.weight_bf16);
-      y[e] = o[e] * rstd * w * silu;
-    }
-    store4_bf16<kVecAct>(p.out + (token * HV + head) * kDim + 4 * lane, y);
+    gated_rmsnorm_store<kVecAct>(sh_o[t], z, w, p.eps, lane, p.out + ((bos + t) * static_cast<int64_t>(HV) + head) * kDim);
   }
 }
 
-bool aligned(const void* ptr, uintptr_t bytes) {
-  return (reinterpret_cast<uintptr_t>(ptr) % bytes) == 0;
+// ==========================================================================================
+// Streaming kernel: persistent CTAs, TMA bulk prefetch of states into a shared-memory ring.
+// ==========================================================================================
+namespace stream {
+
+constexpr int kStates = 3;                            // state ring depth (64 KiB each)
+constexpr int kActs = kStates + 1;                    // activation ring depth
+constexpr uint64_t kWaitLimitNs = 1000000000ull;      // 1 s bound on every mbarrier wait
+
+enum ItemKind : int { kSkip = 0, kZero = 1, kRun = 2 };
+
+struct ItemInfo {
+  int kind;
+  int n;
+  int bos;
+  int pad;
+  int dst[kMaxTokens];
+  float decay[kMaxTokens];
+  float beta[kMaxTokens];
+};
+
+struct ActStage {
+  __nv_bfloat16 q[kMaxTokens][kDim];
+  __nv_bfloat16 k[kMaxTokens][kDim];
+  __nv_bfloat16 v[kMaxTokens][kDim];
+  __nv_bfloat16 z[kMaxTokens][kDim];
+  ItemInfo info;
+};
+
+struct Smem {
+  static constexpr int kStateStages = kStates;
+  static constexpr int kActStages = kActs;
+  float state[kStates][kHeadElems];
+  ActStage act[kActs];
+  float out[2][kMaxTokens][kDim];
+  unsigned long long full[kStates];
+  unsigned long long empty_state[kStates];
+  unsigned long long empty_act[kActs];
+  unsigned long long out_full[2];   // all consumer warps wrote their rows of out[b]
+  unsigned long long out_empty[2];  // all consumer warps are past the epilogue that read out[b]
+  int abort;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* ptr) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
 }
+
+__device__ __forceinline__ void mbar_init(unsigned long long* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(unsigned long long* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(unsigned long long* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Waits for the phase of `bar` with the given parity; false once kWaitLimitNs has passed.
+__device__ __noinline__ bool mbar_wait(unsigned long long* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = global_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_ns() - start > kWaitLimitNs) return false;
+  }
+  return true;
+}
+
+// Non-multicast TMA bulk copy global -> this CTA's shared memory, completing on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, unsigned long long* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// Bounded wait whose outcome is the same for every lane of the warp.
+__device__ __forceinline__ bool warp_wait(unsigned long long* bar, uint32_t parity) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+}
+
+template <class S>
+__device__ __forceinline__ void set_abort(S& sm) {
+  atomicOr(&g_decode_faults, LD_FAULT_WAIT_TIMEOUT);
+  *reinterpret_cast<volatile int*>(&sm.abort) = 1;
+}
+
+template <class S>
+__device__ __forceinline__ bool aborted(const S& sm) { return *reinterpret_cast<const volatile int*>(&sm.abort) != 0; }
+
+// Everything the producer needs to issue one item, resolved ahead of time by one lane.
+struct ItemPlan {
+  int kind;
+  int src;
+  int bos;
+  int n;
+  int dst[kMaxTokens];
+  float decay[kMaxTokens];
+  float beta[kMaxTokens];
+};
+
+// Resolves an item's source slot, token range, destination slots and gates (the validity rules of
+// the reference kernel, gdn_decode.cu:150-168 and :303-316).  Items past the end plan as kSkip.
+__device__ ItemPlan plan_item(const DecodeArgs& p, int64_t item) {
+  ItemPlan plan;
+  plan.kind = kSkip;
+  plan.src = 0;
+  plan.bos = 0;
+  plan.n = 0;
+#pragma unroll
+  for (int t = 0; t < kMaxTokens; ++t) {
+    plan.dst[t] = 0;
+    plan.decay[t] = 0.0f;
+    plan.beta[t] = 0.0f;
+  }
+  if (item >= p.total_items) return plan;
+  const int HV = p.num_v_heads;
+  const int W = p.width;
+  const int request = static_cast<int>(item / HV);
+  const int head = static_cast<int>(item - static_cast<int64_t>(request) * HV);
+  const int bos = p.cu[request];
+  const int eos = p.cu[request + 1];
+  const int acc = p.accepted[request];
+  const int n = eos - bos;
+  plan.bos = bos;
+  plan.n = n;
+  if (n <= 0) return plan;
+  if (bos < 0 || static_cast<int64_t>(eos) > p.n_tokens) {
+    atomicOr(&g_decode_faults, LD_FAULT_DECODE_TOKENS);
+    return plan;
+  }
+  const int src = (acc >= 1 && acc <= W) ? p.indices[request * W + acc - 1] : 0;
+  if (src <= 0 || n > W || src >= p.n_slots) {
+    if (n > W) atomicOr(&g_decode_faults, LD_FAULT_DECODE_TOKENS);
+    if (src >= p.n_slots) atomicOr(&g_decode_faults, LD_FAULT_DECODE_SLOT_RANGE);
+    plan.kind = kZero;
+    return plan;
+  }
+  plan.kind = kRun;
+  plan.src = src;
+#pragma unroll
+  for (int t = 0; t < kMaxTokens; ++t) {
+    if (t < n) {
+      int dst = p.indices[request * W + t];
+      if (dst >= p.n_slots) {
+        atomicOr(&g_decode_faults, LD_FAULT_DECODE_SLOT_RANGE);
+        dst = 0;
+      }
+      plan.dst[t] = dst;
+      token_gates(p, bos + t, head, plan.decay[t], plan.beta[t]);
+    }
+  }
+  return plan;
+}
+
+// Producer warp.  Every 32 items, lane i plans the CTA's item k + i, so the dependent metadata
+// loads of 32 items share one round of memory latency; items are then issued in order from the
+// planning lane's registers: wait for a free stage, publish the plan, start the TMA bulk copies.
+template <class S>
+__device__ void produce(const DecodeArgs& p, S& sm, int lane) {
+  constexpr int kStates = S::kStateStages;
+  constexpr int kActs = S::kActStages;
+  const int HV = p.num_v_heads;
+  const int H = p.num_k_heads;
+  ItemPlan mine;
+  int k = 0;
+  for (int64_t item = blockIdx.x; item < p.total_items; item += gridDim.x, ++k) {
+    if (aborted(sm)) break;
+    const int owner = k & 31;
+    if (owner == 0) mine = plan_item(p, item + static_cast<int64_t>(lane) * gridDim.x);
+    const int kind = __shfl_sync(0xffffffffu, mine.kind, owner);
+    const int src = __shfl_sync(0xffffffffu, mine.src, owner);
+    const int bos = __shfl_sync(0xffffffffu, mine.bos, owner);
+    const int n = __shfl_sync(0xffffffffu, mine.n, owner);
+    int dst[kMaxTokens];
+    float decay[kMaxTokens], beta[kMaxTokens];
+#pragma unroll
+    for (int t = 0; t < kMaxTokens; ++t) {
+      dst[t] = __shfl_sync(0xffffffffu, mine.dst[t], owner);
+      decay[t] = __shfl_sync(0xffffffffu, mine.decay[t], owner);
+      beta[t] = __shfl_sync(0xffffffffu, mine.beta[t], owner);
+    }
+    const int head = static_cast<int>(item % HV);
+
+    const int s = k % kStates;
+    const int a = k % kActs;
+    bool ok = true;
+    if (k >= kStates) ok = warp_wait(&sm.empty_state[s], ((k / kStates) - 1) & 1);
+    if (ok && k >= kActs) ok = warp_wait(&sm.empty_act[a], ((k / kActs) - 1) & 1);
+    if (!ok) {
+      if (lane == 0) set_abort(sm);
+      break;
+    }
+    if (lane == 0) {
+      ItemInfo& info = sm.act[a].info;
+#pragma unroll
+      for (int t = 0; t < kMaxTokens; ++t) {
+        info.dst[t] = dst[t];
+        info.decay[t] = decay[t];
+        info.beta[t] = beta[t];
+      }
+      info.kind = kind;
+      info.n = n;
+      info.bos = bos;
+      if (kind == kRun) {
+        mbar_arrive_expect_tx(&sm.full[s], kHeadBytes + n * 4 * kRowBytes);
+        const float* src_head = p.state + static_cast<int64_t>(src) * p.slot_stride + static_cast<int64_t>(head) * kHeadElems;
+        bulk_load(sm.state[s], src_head, kHeadBytes, &sm.full[s]);
+        const int key_head = head / p.heads_ratio;
+        for (int t = 0; t < n; ++t) {
+          const int64_t token = bos + t;
+          const __nv_bfloat16* row = p.qkv + token * p.qkv_row;
+          bulk_load(sm.act[a].q[t], row + key_head * kDim, kRowBytes, &sm.full[s]);
+          bulk_load(sm.act[a].k[t], row + (H + key_head) * kDim, kRowBytes, &sm.full[s]);
+          bulk_load(sm.act[a].v[t], row + (2 * H + head) * kDim, kRowBytes, &sm.full[s]);
+          bulk_load(sm.act[a].z[t], p.gate + token * p.gate_row + head * kDim, kRowBytes, &sm.full[s]);
+        }
+      } else {
+        mbar_arrive(&sm.full[s]);
+      }
+    }
+    __syncwarp();
+  }
+  // Drain: every bulk copy this warp issued has landed before the CTA may exit.
+  if (lane == 0) {
+    for (int kk = k > kStates ? k - kStates : 0; kk < k; ++kk) {
+      if (!mbar_wait(&sm.full[kk % kStates], (kk / kStates) & 1)) {
+        set_abort(sm);
+        break;
+      }
+    }
+  }
+}
+
+// Reads this lane's 16 columns {32c + 4j ..} of a bf16 head row from shared memory.
+__device__ __forceinline__ void load_row_cols(const __nv_bfloat16* row, int j, float4 (&v)[kVecPerRow], float& sq) {
+  sq = 0.0f;
+#pragma unroll
+  for (int c = 0; c < kVecPerRow; ++c) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(row + c * 4 * kLanesPerRow + 4 * j);
+    v[c] = make_float4(bf16_lo(raw.x), bf16_hi(raw.x), bf16_lo(raw.y), bf16_hi(raw.y));
+    sq += v[c].x * v[c].x + v[c].y * v[c].y + v[c].z * v[c].z + v[c].w * v[c].w;
+  }
+}
+
+template <int kRows>
+__device__ void consume(const DecodeArgs& p, Smem& sm, int tid) {
+  constexpr int kConsumers = Tile<kRows>::kThreads;
+  constexpr int kRowGroups = Tile<kRows>::kRowGroups;
+  const int HV = p.num_v_heads;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int j = tid & (kLanesPerRow - 1);
+  const int g = tid / kLanesPerRow;
+  float w[4] = {0.f, 0.f, 0.f, 0.f};
+  if (warp < kMaxTokens) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) w[e] = load_param(p.weight, 4 * lane + e, p.weight_bf16);
+  }
+  int k = 0;
+  int runs = 0;
+  for (int64_t item = blockIdx.x; item < p.total_items; item += gridDim.x, ++k) {
+    const int s = k % kStates;
+    const int a = k % kActs;
+    if (!warp_wait(&sm.full[s], (k / kStates) & 1)) {
+      if (lane == 0) set_abort(sm);
+      break;
+    }
+    const ItemInfo& info = sm.act[a].info;
+    const int kind = info.kind;
+    const int n = info.n;
+    const int64_t bos = info.bos;
+    const int head = static_cast<int>(item % HV);
+    if (kind != kRun) {
+      if (kind == kZero) {
+        for (int idx = tid; idx < n * kDim; idx += kConsumers) {
+          const int64_t token = bos + idx / kDim;
+          p.out[(token * HV + head) * kDim + (idx % kDim)] = __float2bfloat16_rn(0.0f);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&sm.empty_state[s]);
+        mbar_arrive(&sm.empty_act[a]);
+      }
+      continue;
+    }
+
+    // State ring -> registers; the stage is released as soon as every warp has its tile.
+    float4 tile[kRows][kVecPerRow];
+    load_tile<kRows>(sm.state[s], g, j, tile);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.empty_state[s]);
+
+    const ActStage& act = sm.act[a];
+    const int buf = runs & 1;
+    const int use = runs >> 1;
+    // out[buf] was last read by the epilogue two run items ago.
+    if (use > 0 && !warp_wait(&sm.out_empty[buf], (use - 1) & 1)) {
+      if (lane == 0) set_abort(sm);
+      break;
+    }
+    float* o_buf = &sm.out[buf][0][0];
+    const int64_t head_offset = static_cast<int64_t>(head) * kHeadElems;
+    for (int t = 0; t < n; ++t) {
+      float4 kv[kVecPerRow], qv[kVecPerRow];
+      float k_sq, q_sq;
+      load_row_cols(act.k[t], j, kv, k_sq);
+      load_row_cols(act.q[t], j, qv, q_sq);
+      k_sq = row_sum(k_sq);
+      q_sq = row_sum(q_sq);
+      // L2 norm in fp32 as gdn.py:98-99; q then scaled by K^-1/2 as gdn.py:101.
+      const float k_inv = 1.0f / sqrtf(k_sq + 1e-6f);
+      const float q_inv = 1.0f / sqrtf(q_sq + 1e-6f);
+#pragma unroll
+      for (int c = 0; c < kVecPerRow; ++c) {
+        kv[c] = make_float4(kv[c].x * k_inv, kv[c].y * k_inv, kv[c].z * k_inv, kv[c].w * k_inv);
+        qv[c] = make_float4(qv[c].x * q_inv * p.q_scale, qv[c].y * q_inv * p.q_scale, qv[c].z * q_inv * p.q_scale,
+                            qv[c].w * q_inv * p.q_scale);
+      }
+      float vrow[kRows], o[kRows];
+#pragma unroll
+      for (int i = 0; i < kRows; ++i) vrow[i] = __bfloat162float(act.v[t][g + i * kRowGroups]);
+      tile_step<kRows>(tile, kv, qv, vrow, info.decay[t], info.beta[t], o);
+      if (j == 0) {
+#pragma unroll
+        for (int i = 0; i < kRows; ++i) {
+          o_buf[t * kDim + g + i * kRowGroups] = __bfloat162float(__float2bfloat16_rn(o[i]));
+        }
+      }
+      const int dst = info.dst[t];
+      if (dst > 0) store_tile<kRows>(p.state + static_cast<int64_t>(dst) * p.slot_stride + head_offset, g, j, tile);
+    }
+    float z[4] = {0.f, 0.f, 0.f, 0.f};
+    if (warp < n) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(&act.z[warp][4 * lane]);
+      z[0] = bf16_lo(raw.x);
+      z[1] = bf16_hi(raw.x);
+      z[2] = bf16_lo(raw.y);
+      z[3] = bf16_hi(raw.y);
+    }
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive(&sm.empty_act[a]);
+      mbar_arrive(&sm.out_full[buf]);
+    }
+    if (warp < n) {
+      if (!warp_wait(&sm.out_full[buf], use & 1)) {  // every row's output of this item is in o_buf
+        if (lane == 0) set_abort(sm);
+        break;
+      }
+      gated_rmsnorm_store<true>(o_buf + warp * kDim, z, w, p.eps, lane,
+                                p.out + ((bos + warp) * HV + head) * kDim);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.out_empty[buf]);
+    ++runs;
+  }
+}
+
+// Block: Tile<kRows>::kThreads consumer threads followed by one producer warp, one CTA per SM.
+// The register cap keeps the block launchable: warps are spread over the SM's four 16 K-register
+// sub-partitions, so 17 warps (2-row tile) allow 96 registers per thread and 9 warps allow 168.
+template <int kRows>
+__global__ void __maxnreg__(kRows == 2 ? 96 : 168) gdn_decode_stream_kernel(const DecodeArgs p) {
+  constexpr int kConsumers = Tile<kRows>::kThreads;
+  constexpr int kConsumerWarps = kConsumers / 32;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    for (int s = 0; s < kStates; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty_state[s], kConsumerWarps);
+    }
+    for (int a = 0; a < kActs; ++a) mbar_init(&sm.empty_act[a], kConsumerWarps);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.out_full[b], kConsumerWarps);
+      mbar_init(&sm.out_empty[b], kConsumerWarps);
+    }
+    sm.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  __syncthreads();
+  if (tid >= kConsumers) {
+    produce(p, sm, tid & 31);
+  } else {
+    consume<kRows>(p, sm, tid);
+  }
+}
+
+
+// ------------------------------------------------------------------------------------------
+// TMA-store variant.  The SM's global-store port moves about 61 GB/s, so writing a 64 KiB
+// state from registers occupies the consumer warps for over a microsecond per step, during
+// which their ALUs idle (and during compute the port idles).  Here each step's state is
+// written into a shared-memory staging tile instead and a dedicated storer warp drains it
+// with one TMA bulk store (cp.async.bulk.global.shared::cta) while the consumer warps go on
+// computing.  Two load stages plus the staging tile fit in shared memory.
+// ------------------------------------------------------------------------------------------
+namespace ts {
+
+constexpr int kConsumers = Tile<4>::kThreads;    // 256
+constexpr int kConsumerWarps = kConsumers / 32;  // 8
+constexpr int kThreads = kConsumers + 64;        // + producer warp + storer warp
+
+// kLoads TMA load stages and kStaging staging tiles: (2, 1) for decode, where prefetch depth
+// matters, and (1, 2) for multi-token verify, where each item makes several stores and a second
+// staging tile lets one step's drain overlap the next step's compute.
+template <int kLoads, int kStaging>
+struct Smem {
+  static constexpr int kStateStages = kLoads;
+  static constexpr int kActStages = kLoads + 1;
+  float state[kLoads][kHeadElems];
+  float staging[kStaging][kHeadElems];
+  ActStage act[kLoads + 1];
+  float out[2][kMaxTokens][kDim];
+  float* store_dst[2];                   // destination of staging event e (entry e & 1); null ends the storer
+  unsigned long long full[kLoads];
+  unsigned long long empty_state[kLoads];
+  unsigned long long empty_act[kLoads + 1];
+  unsigned long long out_full[2];
+  unsigned long long out_empty[2];
+  unsigned long long tile_ready[kStaging];    // every consumer warp has written its part of the tile
+  unsigned long long staging_free[kStaging];  // the storer's bulk store has read the tile out
+  int abort;
+};
+
+template <int kLoads, int kStaging>
+__device__ void consume(const DecodeArgs& p, Smem<kLoads, kStaging>& sm, int tid) {
+  constexpr int kRows = 4;
+  constexpr int kRowGroups = Tile<kRows>::kRowGroups;
+  constexpr int kActRing = kLoads + 1;
+  const int HV = p.num_v_heads;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int j = tid & (kLanesPerRow - 1);
+  const int g = tid / kLanesPerRow;
+  float w[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) w[e] = load_param(p.weight, 4 * lane + e, p.weight_bf16);
+  int k = 0;
+  int runs = 0;
+  uint32_t events = 0;  // staging events issued (same count in every consumer warp)
+  bool failed = false;
+  for (int64_t item = blockIdx.x; item < p.total_items; item += gridDim.x, ++k) {
+    const int s = k % kLoads;
+    const int a = k % kActRing;
+    if (!warp_wait(&sm.full[s], (k / kLoads) & 1)) {
+      failed = true;
+      break;
+    }
+    const ItemInfo& info = sm.act[a].info;
+    const int kind = info.kind;
+    const int n = info.n;
+    const int64_t bos = info.bos;
+    const int head = static_cast<int>(item % HV);
+    if (kind != kRun) {
+      if (kind == kZero) {
+        for (int idx = tid; idx < n * kDim; idx += kConsumers) {
+          const int64_t token = bos + idx / kDim;
+          p.out[(token * HV + head) * kDim + (idx % kDim)] = __float2bfloat16_rn(0.0f);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&sm.empty_state[s]);
+        mbar_arrive(&sm.empty_act[a]);
+      }
+      continue;
+    }
+
+    float4 tile[kRows][kVecPerRow];
+    load_tile<kRows>(sm.state[s], g, j, tile);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.empty_state[s]);
+
+    const ActStage& act = sm.act[a];
+    const int buf = runs & 1;
+    const int use = runs >> 1;
+    if (use > 0 && !warp_wait(&sm.out_empty[buf], (use - 1) & 1)) {
+      failed = true;
+      break;
+    }
+    float* o_buf = &sm.out[buf][0][0];
+    const int64_t head_offset = static_cast<int64_t>(head) * kHeadElems;
+    for (int t = 0; t < n; ++t) {
+      float4 kv[kVecPerRow], qv[kVecPerRow];
+      float k_sq, q_sq;
+      load_row_cols(act.k[t], j, kv, k_sq);
+      load_row_cols(act.q[t], j, qv, q_sq);
+      k_sq = row_sum(k_sq);
+      q_sq = row_sum(q_sq);
+      // L2 norm in fp32 as gdn.py:98-99; q then scaled by K^-1/2 as gdn.py:101.
+      const float k_inv = 1.0f / sqrtf(k_sq + 1e-6f);
+      const float q_inv = 1.0f / sqrtf(q_sq + 1e-6f);
+#pragma unroll
+      for (int c = 0; c < kVecPerRow; ++c) {
+        kv[c] = make_float4(kv[c].x * k_inv, kv[c].y * k_inv, kv[c].z * k_inv, kv[c].w * k_inv);
+        qv[c] = make_float4(qv[c].x * q_inv * p.q_scale, qv[c].y * q_inv * p.q_scale, qv[c].z * q_inv * p.q_scale,
+                            qv[c].w * q_inv * p.q_scale);
+      }
+      float vrow[kRows], o[kRows];
+#pragma unroll
+      for (int i = 0; i < kRows; ++i) vrow[i] = __bfloat162float(act.v[t][g + i * kRowGroups]);
+      tile_step<kRows>(tile, kv, qv, vrow, info.decay[t], info.beta[t], o);
+      if (j == 0) {
+#pragma unroll
+        for (int i = 0; i < kRows; ++i) o_buf[t * kDim + g + i * kRowGroups] = __bfloat162float(__float2bfloat16_rn(o[i]));
+      }
+      const int dst = info.dst[t];
+      if (dst > 0) {
+        // Staging tile b is free once the storer has read out event `events - kStaging`.
+        const int b = events % kStaging;
+        if (events >= kStaging && !warp_wait(&sm.staging_free[b], ((events / kStaging) - 1) & 1)) {
+          failed = true;
+          break;
+        }
+        store_tile<kRows>(sm.staging[b], g, j, tile);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> TMA reads
+        if (tid == 0) sm.store_dst[events & 1] = p.state + static_cast<int64_t>(dst) * p.slot_stride + head_offset;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.tile_ready[b]);
+        ++events;
+      }
+    }
+    if (failed) break;
+    // The epilogue of token t of this item runs on warp (runs + t) mod 8, spreading the
+    // gated-RMSNorm work over all consumer warps instead of loading warp 0 with every token.
+    const int my_token = (warp - runs % kConsumerWarps + kConsumerWarps) % kConsumerWarps;
+    const bool epilogue = my_token < n;
+    float z[4] = {0.f, 0.f, 0.f, 0.f};
+    if (epilogue) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(&act.z[my_token][4 * lane]);
+      z[0] = bf16_lo(raw.x);
+      z[1] = bf16_hi(raw.x);
+      z[2] = bf16_lo(raw.y);
+      z[3] = bf16_hi(raw.y);
+    }
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive(&sm.empty_act[a]);
+      mbar_arrive(&sm.out_full[buf]);
+    }
+    if (epilogue) {
+      if (!warp_wait(&sm.out_full[buf], use & 1)) {  // every row's output of this item is in o_buf
+        failed = true;
+        break;
+      }
+      gated_rmsnorm_store<true>(o_buf + my_token * kDim, z, w, p.eps, lane,
+                                p.out + ((bos + my_token) * HV + head) * kDim);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.out_empty[buf]);
+    ++runs;
+  }
+  if (failed) {
+    if (lane == 0) set_abort(sm);
+    return;
+  }
+  // A final staging event with a null destination tells the storer to finish.
+  if (events >= kStaging &&
+      !warp_wait(&sm.staging_free[events % kStaging], ((events / kStaging) - 1) & 1)) {
+    if (lane == 0) set_abort(sm);
+    return;
+  }
+  if (tid == 0) sm.store_dst[events & 1] = nullptr;
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&sm.tile_ready[events % kStaging]);
+}
+
+// Storer warp (one lane): drains staging event e with a TMA bulk store of tile e % kStaging.
+// With two tiles it keeps one store in flight while waiting for the next tile.
+template <int kLoads, int kStaging>
+__device__ void store_loop(Smem<kLoads, kStaging>& sm, int lane) {
+  if (lane != 0) return;
+  uint32_t e = 0;
+  for (;; ++e) {
+    const int b = e % kStaging;
+    if (!mbar_wait(&sm.tile_ready[b], (e / kStaging) & 1)) {
+      set_abort(sm);
+      break;
+    }
+    float* dst = sm.store_dst[e & 1];
+    if (dst == nullptr) break;
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_u32(sm.staging[b])),
+                 "r"(kHeadBytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    if constexpr (kStaging == 1) {
+      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      mbar_arrive(&sm.staging_free[0]);
+    } else {
+      // Event e - 1 has been read out once at most one group (event e) is still reading.
+      if (e > 0) {
+        asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+        mbar_arrive(&sm.staging_free[(e - 1) % kStaging]);
+      }
+    }
+  }
+  if constexpr (kStaging > 1) {
+    if (e > 0) {
+      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      mbar_arrive(&sm.staging_free[(e - 1) % kStaging]);
+    }
+  }
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // every bulk store has completed
+}
+
+// Block: 256 consumer threads, one producer warp, one storer warp; one CTA per SM.
+template <int kLoads, int kStaging>
+__global__ void __maxnreg__(168) gdn_decode_tmastore_kernel(const DecodeArgs p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  using S = Smem<kLoads, kStaging>;
+  S& sm = *reinterpret_cast<S*>(smem_raw);
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    for (int s = 0; s < kLoads; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty_state[s], kConsumerWarps);
+    }
+    for (int a = 0; a < kLoads + 1; ++a) mbar_init(&sm.empty_act[a], kConsumerWarps);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.out_full[b], kConsumerWarps);
+      mbar_init(&sm.out_empty[b], kConsumerWarps);
+    }
+    for (int b = 0; b < kStaging; ++b) {
+      mbar_init(&sm.tile_ready[b], kConsumerWarps);
+      mbar_init(&sm.staging_free[b], 1);
+    }
+    sm.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  __syncthreads();
+  if (tid < kConsumers) {
+    consume<kLoads, kStaging>(p, sm, tid);
+  } else if (tid < kConsumers + 32) {
+    produce(p, sm, tid & 31);
+  } else {
+    store_loop<kLoads, kStaging>(sm, tid & 31);
+  }
+}
+
+}  // namespace ts
+
+}  // namespace stream
+
+bool aligned(const void* ptr, uintptr_t bytes) { return (reinterpret_cast<uintptr_t>(ptr) % bytes) == 0; }
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  int sms = 0;
+  bool stream_ready = false;
+};
+
+// Per-device launch facts: SM count, and the shared-memory opt-in of the streaming kernel.
+int device_info(DeviceInfo& out) {
+  static std::mutex mutex;
+  static DeviceInfo infos[kMaxDevices];
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return set_error(LD_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(err));
+  if (device < 0 || device >= kMaxDevices) return set_error(LD_ERR_INVALID, "device index %d unsupported", device);
+  std::lock_guard<std::mutex> lock(mutex);
+  DeviceInfo& info = infos[device];
+  if (!info.stream_ready) {
+    err = cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, device);
+    if (err != cudaSuccess) return set_error(LD_ERR_CUDA, "SM count: %s", cudaGetErrorString(err));
+    for (auto kernel : {stream::gdn_decode_stream_kernel<4>, stream::gdn_decode_stream_kernel<2>}) {
+      err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(sizeof(stream::Smem)));
+      if (err != cudaSuccess) return set_error(LD_ERR_CUDA, "shared-memory opt-in: %s", cudaGetErrorString(err));
+    }
+    err = cudaFuncSetAttribute(stream::ts::gdn_decode_tmastore_kernel<2, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(sizeof(stream::ts::Smem<2, 1>)));
+    if (err == cudaSuccess) {
+      err = cudaFuncSetAttribute(stream::ts::gdn_decode_tmastore_kernel<1, 2>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(sizeof(stream::ts::Smem<1, 2>)));
+    }
+    if (err != cudaSuccess) return set_error(LD_ERR_CUDA, "shared-memory opt-in: %s", cudaGetErrorString(err));
+    info.stream_ready = true;
+  }
+  out = info;
+  return LD_OK;
+}
+
+std::atomic<int> g_kernel_override{LD_DECODE_KERNEL_AUTO};
 
 }  // namespace
 
@@ -428,6 +1189,7 @@ extern "C" int ld_decode(const void* qkv, int64_t qkv_row_stride, const void* a,
   args.weight = weight;
   args.out = static_cast<__nv_bfloat16*>(out);
   args.n_tokens = n_tokens;
+  args.total_items = n_requests * num_v_heads;
   args.width = static_cast<int>(width);
   args.num_k_heads = static_cast<int>(num_k_heads);
   args.num_v_heads = static_cast<int>(num_v_heads);
@@ -438,18 +1200,56 @@ extern "C" int ld_decode(const void* qkv, int64_t qkv_row_stride, const void* a,
   args.q_scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(LD_HEAD_DIM)));
   args.eps = eps;
 
-  const bool vec_act = aligned(qkv, 8) && qkv_row_stride % 4 == 0 && aligned(gate, 8) &&
-                       gate_row_stride % 4 == 0 && aligned(out, 8);
-  const dim3 grid(static_cast<unsigned int>(n_requests * num_v_heads));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (vec_act) {
-    gdn_decode_kernel<true><<<grid, kThreads, 0, s>>>(args);
+  // TMA bulk copies need 16-byte aligned sources: qkv and gate rows must start on 16 bytes.
+  const bool bulk_ok = aligned(qkv, 16) && qkv_row_stride % 8 == 0 && aligned(gate, 16) &&
+                       gate_row_stride % 8 == 0 && aligned(out, 8);
+  int variant = g_kernel_override.load(std::memory_order_relaxed);
+  if (variant == LD_DECODE_KERNEL_AUTO) {
+    // Measured on B200 (BASELINE configs 2 and 3): the streaming kernel is fastest for one-token
+    // decode, the one-CTA-per-item kernel for multi-token verify, whose four state writes per
+    // item favour its two resident CTAs per SM.
+    variant = width == 1 ? LD_DECODE_KERNEL_STREAM_4ROW : LD_DECODE_KERNEL_ROWREG;
+  }
+  if (!bulk_ok) variant = LD_DECODE_KERNEL_ROWREG;
+  if (variant != LD_DECODE_KERNEL_ROWREG) {
+    DeviceInfo info;
+    const int rc = device_info(info);
+    if (rc != LD_OK) return rc;
+    const unsigned int grid = static_cast<unsigned int>(std::min<int64_t>(args.total_items, info.sms));
+    if (variant == LD_DECODE_KERNEL_STREAM_2ROW) {
+      stream::gdn_decode_stream_kernel<2><<<grid, Tile<2>::kThreads + 32, sizeof(stream::Smem), s>>>(args);
+    } else if (variant == LD_DECODE_KERNEL_TMA_STORE) {
+      if (width == 1) {
+        stream::ts::gdn_decode_tmastore_kernel<2, 1><<<grid, stream::ts::kThreads, sizeof(stream::ts::Smem<2, 1>), s>>>(
+            args);
+      } else {
+        stream::ts::gdn_decode_tmastore_kernel<1, 2><<<grid, stream::ts::kThreads, sizeof(stream::ts::Smem<1, 2>), s>>>(
+            args);
+      }
+    } else {
+      stream::gdn_decode_stream_kernel<4><<<grid, Tile<4>::kThreads + 32, sizeof(stream::Smem), s>>>(args);
+    }
   } else {
-    gdn_decode_kernel<false><<<grid, kThreads, 0, s>>>(args);
+    const bool vec_act = aligned(qkv, 8) && qkv_row_stride % 4 == 0 && aligned(gate, 8) &&
+                         gate_row_stride % 4 == 0 && aligned(out, 8);
+    const dim3 grid(static_cast<unsigned int>(args.total_items));
+    if (vec_act) {
+      gdn_decode_rowreg_kernel<true><<<grid, Tile<4>::kThreads, 0, s>>>(args);
+    } else {
+      gdn_decode_rowreg_kernel<false><<<grid, Tile<4>::kThreads, 0, s>>>(args);
+    }
   }
   const cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) {
     return set_error(LD_ERR_CUDA, "decode launch failed: %s", cudaGetErrorString(err));
   }
   return ok();
+}
+
+extern "C" int ld_decode_kernel_override(int variant) {
+  if (variant < LD_DECODE_KERNEL_AUTO || variant > LD_DECODE_KERNEL_TMA_STORE) {
+    return ldb::set_error(-LD_ERR_INVALID, "unknown decode kernel variant %d", variant);
+  }
+  return ldb::g_kernel_override.exchange(variant);
 }

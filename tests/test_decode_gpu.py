@@ -21,6 +21,16 @@ from lightdelta_b200.config import BackendConfig
 
 pytestmark = pytest.mark.gpu
 
+VARIANTS = ["tmastore", "stream4", "stream2", "rowreg"]
+
+
+@pytest.fixture(params=VARIANTS)
+def kernel(request, device):
+    """Runs the test once per decode kernel variant (all must match the oracle)."""
+    previous = capi.set_decode_kernel(request.param)
+    yield request.param
+    capi.set_decode_kernel(previous)
+
 
 def _golden(name):
     return np.load(cases.__file__.replace("cases.py", f"{name}.npz"))
@@ -56,7 +66,7 @@ def check_against_oracle(t, host, num_k_heads, touched=None, what="decode"):
 
 @pytest.mark.parametrize("path", ["torch_op", "capi"])
 @pytest.mark.parametrize("name", [c["name"] for c in cases.BACKEND_CASES])
-def test_decode_matches_reference_golden(device, name, path):
+def test_decode_matches_reference_golden(device, kernel, name, path):
     """Indexed decode on the reference geometry (H=16, HV=48) against the reference backend's own
     results and against the oracle on the whole pool."""
     spec = cases.spec_by_name(name)
@@ -79,7 +89,7 @@ def test_decode_matches_reference_golden(device, name, path):
 
 @pytest.mark.parametrize("width", [1, 2, 3, 4])
 @pytest.mark.parametrize("state_io", ["packed", "indexed"])
-def test_backend_matches_oracle(device, width, state_io):
+def test_backend_matches_oracle(device, kernel, width, state_io):
     """Reference tests/test_gdn.py:58-75 at HV=32: mixed accepted counts and a padding request."""
     case = workloads.make_decode_case(4, width, 24, device=device, seed=100 + width, accepted="ones")
     case.accepted.copy_(torch.arange(4, device=device, dtype=torch.int32) % width + 1)
@@ -94,7 +104,7 @@ def test_backend_matches_oracle(device, width, state_io):
 
 
 @pytest.mark.parametrize("state_io", ["packed", "indexed"])
-def test_graph_replay_changed_state_indices(device, state_io):
+def test_graph_replay_changed_state_indices(device, kernel, state_io):
     """Reference tests/test_gdn.py:78-102: capture once, then change slots and accepted counts."""
     case = workloads.make_decode_case(2, 3, 16, device=device, seed=7)
     t = case.kwargs()
@@ -131,7 +141,7 @@ def test_packed_and_indexed_are_bit_identical(device):
 
 
 @pytest.mark.parametrize("config", ["config2", "config3"])
-def test_baseline_config_full_size_matches_oracle(device, config):
+def test_baseline_config_full_size_matches_oracle(device, kernel, config):
     """BASELINE config 2 (B=256, T=1, pool 1024 x [32,128,128]) and config 3 (B=64, T=4 verify,
     accepted ~ U{1..4}) at full size: every touched slot and every output against the oracle."""
     case = workloads.config2(device) if config == "config2" else workloads.config3(device)
@@ -150,7 +160,7 @@ def test_baseline_config_full_size_matches_oracle(device, config):
 
 
 @pytest.mark.parametrize("heads", [(16, 16), (8, 32), (16, 48), (4, 12)])
-def test_head_geometries(device, heads):
+def test_head_geometries(device, kernel, heads):
     h, hv = heads
     case = workloads.make_decode_case(3, 2, 12, device=device, seed=h * 100 + hv, num_k_heads=h, num_v_heads=hv,
                                       accepted="uniform", state_scale=0.1)
@@ -177,7 +187,7 @@ def test_unaligned_activations_use_the_scalar_path(device):
     check_against_oracle(t, host, base.num_k_heads, what="unaligned")
 
 
-def test_invalid_requests_and_fault_word(device):
+def test_invalid_requests_and_fault_word(device, kernel):
     """Zero outputs and no writes for a bad accepted count, a request longer than the window and an
     out-of-range source slot; nothing for a request with no tokens; out-of-range destinations are
     skipped.  Each raises its bit in the device fault word."""
@@ -203,7 +213,7 @@ def test_invalid_requests_and_fault_word(device):
     assert_state_close(case.pool.cpu().numpy(), host["pool"], "invalid requests pool")
 
 
-def test_too_many_tokens_sets_the_token_fault(device):
+def test_too_many_tokens_sets_the_token_fault(device, kernel):
     case = workloads.make_decode_case(2, 2, 8, device=device, seed=6)
     capi.fault_flags(clear=True)
     case.cu.copy_(torch.tensor([0, 3, 4], device=device, dtype=torch.int32))  # request 0 has 3 tokens > width 2
@@ -217,7 +227,7 @@ def test_too_many_tokens_sets_the_token_fault(device):
     assert torch.equal(case.pool[slot_r0], before[slot_r0])
 
 
-def test_repeated_in_place_decode(device):
+def test_repeated_in_place_decode(device, kernel):
     """Three consecutive in-place decode steps (source slot == destination slot) track the oracle."""
     case = workloads.make_decode_case(16, 1, 40, device=device, seed=12)
     t = case.kwargs()

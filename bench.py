@@ -7,6 +7,8 @@ Workloads (the default is the one the headline metric is quote
   decode  config 2: indexed decode, 256 sequences per GPU, T=1, pool of 1024 fp32 slots [32,128,128]
   verify  config 3: MTP verify, 64 sequences per GPU, T=4, accepted ~ U{1..4}
   copy    config 4: gather 512 slots of a 2048-slot layer pool, scatter them to a permuted set
+  stacked config 5: 48 layers of T=4 verify over 2048 sequences sharded across the ranks (strong
+          scaling), replayed as one CUDA graph per step; run it with a few --steps (~0.2 s each)
 A step is one launch of the op over that batch.  Under torchrun every rank runs the same
 per-GPU workload on its own slot shard (weak scaling, no data-path collective); the
 rank-local device times are combined as their maximum.  Rank 0 prints one JSON line.
@@ -48,7 +50,7 @@ def parse_args(argv=None):
     p.add_argument("--steps", type=int, default=4000)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--workload", choices=("decode", "verify", "copy"), default="decode")
+    p.add_argument("--workload", choices=("decode", "verify", "copy", "stacked"), default="decode")
     p.add_argument("--e2e-steps", type=int, default=200)
     p.add_argument("--decode-kernel", choices=("auto", "tmastore", "stream4", "stream2", "rowreg"), default="auto",
                    help="decode kernel variant (all compute the same results)")
@@ -239,6 +241,40 @@ def run_ours(args, dist: Dist) -> dict | None:
                   "sequences_per_gpu": requests, "tokens_per_sequence": width, "num_k_heads": h,
                   "num_v_heads": hv, "head_dim": 128, "pool_slots": case.pool.shape[0],
                   "state_dtype": "fp32", "activation_dtype": "bf16", "decode_kernel": args.decode_kernel}
+    elif args.workload == "stacked":
+        from lightdelta_b200 import sharding
+
+        total_sequences, layers, width = 2048, 48, 4
+        local = len(sharding.shard_range(total_sequences, dist.rank, dist.world))
+        free, _ = torch.cuda.mem_get_info(device)
+        activations = layers * local * width * 40 * 1024  # proj + out + temporaries per token-layer
+        wl = workloads.stacked_workload(device, local, layers=layers, width=width, seed=5 + seed,
+                                        max_pool_bytes=max(0, free - activations - (8 << 30)))
+        side = torch.cuda.Stream(device)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                for c in wl.layers:
+                    torch.ops.lightdelta.decode(*c.op_args())
+        stream.wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for c in wl.layers:
+                torch.ops.lightdelta.decode(*c.op_args())
+        torch.cuda.synchronize()
+
+        def fn():
+            graph.replay()
+
+        bytes_per_launch = wl.step_bytes() // layers
+        touched = wl.step_bytes()
+        units_per_step, unit = local * width, "tokens/s"
+        case = None
+        config = {"workload": "config5_stacked_verify", "layers": layers, "sequences_total": total_sequences,
+                  "sequences_per_gpu": local, "tokens_per_sequence": width, "num_k_heads": 16, "num_v_heads": 32,
+                  "physical_layer_pools": len(wl.pools),
+                  "pool_slots_per_layer": wl.pools[0].shape[0], "cuda_graph": "one graph of 48 decode launches",
+                  "decode_kernel": args.decode_kernel}
     else:
         pool = torch.empty(2048, 32, 128, 128, device=device)
         pool.normal_(0.0, 0.02)
@@ -260,10 +296,10 @@ def run_ours(args, dist: Dist) -> dict | None:
     sampler.mark(*window)
     clocks = sampler.summary()
     max_ms = dist.max(total_ms)
-    launches_per_step = 2 if args.workload == "copy" else 1
-    kernel_ms = launch_ms / launches_per_step  # copy: two equal-size copies per step
+    launches_per_step = {"copy": 2, "stacked": 48}.get(args.workload, 1)
+    kernel_ms = launch_ms / launches_per_step  # equal-size launches within a step
     achieved_gbs = bytes_per_launch / (kernel_ms * 1e-3) / 1e9
-    value = units_per_step * args.steps * dist.world / (max_ms * 1e-3)
+    value = dist.sum(units_per_step) * args.steps / (max_ms * 1e-3)
     state_gbs_total = dist.sum(bytes_per_launch * launches_per_step * args.steps / (total_ms * 1e-3) / 1e9)
 
     e2e = None
@@ -285,7 +321,7 @@ def run_ours(args, dist: Dist) -> dict | None:
         "warmup": args.warmup,
         "ms_per_step": max_ms / args.steps,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if args.workload == "stacked" else "weak",
         "vs_baseline": None,
         "dtype": "fp32" if args.workload != "copy" else "fp32 (bit copy)",
         "data": "synthetic (seeded, BASELINE config shapes and distributions)",

@@ -132,6 +132,53 @@ def config3(device, seed: int = 3, pool_slots: int = 1 + 256, pool: torch.Tensor
     return make_decode_case(64, 4, pool_slots, device=device, seed=seed, accepted="uniform", pool=pool)
 
 
+@dataclass
+class StackedWorkload:
+    """BASELINE config 5 on one rank: `layers` decode calls per step over the rank's sequences.
+
+    Every layer has its own seeded activations and weights.  Layer l keeps its states in
+    physical pool l % len(pools): when the pools of all 48 layers do not fit in this GPU's
+    memory, layers share physical pools (every pool is far larger than L2, so each layer's
+    state traffic still comes from HBM).
+    """
+
+    layers: list
+    pools: list
+    sequences: int
+    width: int
+
+    def step_bytes(self) -> int:
+        c = self.layers[0]
+        per_layer = decode_algorithmic_bytes(self.sequences, self.width, c.tokens, c.num_k_heads, c.num_v_heads)
+        return per_layer * len(self.layers)
+
+
+def stacked_workload(device, sequences: int, layers: int = 48, width: int = 4, seed: int = 5,
+                     max_pool_bytes: int | None = None, num_k_heads: int = 16,
+                     num_v_heads: int = 32) -> StackedWorkload:
+    """Config 5: `sequences` local sequences, `width`-token MTP verify, `layers` layers."""
+    slot_bytes = num_v_heads * SLOT_HEAD_BYTES
+    pool_slots = 1 + sequences * width
+    pool_bytes = pool_slots * slot_bytes
+    physical = layers
+    if max_pool_bytes is not None:
+        physical = max(1, min(layers, max_pool_bytes // pool_bytes))
+    pools = []
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    for _ in range(physical):
+        pool = torch.empty(pool_slots, num_v_heads, HEAD_DIM, HEAD_DIM, device=device, dtype=torch.float32)
+        pool.normal_(0.0, 0.02, generator=gen)
+        pools.append(pool)
+    cases = [
+        make_decode_case(sequences, width, pool_slots, device=device, seed=seed * 1000 + layer,
+                         num_k_heads=num_k_heads, num_v_heads=num_v_heads, accepted="uniform",
+                         pool=pools[layer % physical])
+        for layer in range(layers)
+    ]
+    return StackedWorkload(layers=cases, pools=pools, sequences=sequences, width=width)
+
+
 def config4_indices(device, seed: int = 4, pool_slots: int = 2048, count: int = 512):
     """Gather 512 distinct slots of 1..2047, scatter them to a permutation of another distinct set."""
     gen = torch.Generator(device=device)

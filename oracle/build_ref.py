@@ -1,0 +1,89 @@
+"""Builds the REFERENCE's own CUDA operator library from its sources, for sm_100a.
+
+TEST INFRASTRUCTURE ONLY.  The reference's csrc/register.cpp, csrc/gdn_decode.cu and
+csrc/state_io.cu (with include/lightdelta/ops.h) are compiled where they lie, unmodified, into
+oracle/_ref/_C.so -- the same torch.library `lightdelta` namespace the product registers, so it
+must be loaded in a process of its own.  The GPU tests use it as a second, independent oracle
+(the reference kernel itself at its HV=48 geometry) and as the kernel to compare against.
+Nothing is copied from the reference tree; nothing is written outside oracle/_ref/.
+
+Run here (where the reference sources exist):  python oracle/build_ref.py [--reference DIR]
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+OUT_DIR = HERE / "_ref"
+OUT = OUT_DIR / "_C.so"
+DEFAULT_REFERENCE = Path("/root/reference")
+SOURCES = ("csrc/register.cpp", "csrc/gdn_decode.cu", "csrc/state_io.cu")
+
+
+def _torch_flags():
+    import torch
+    from torch.utils import cpp_extension
+
+    includes = cpp_extension.include_paths() + ["/usr/local/cuda/include"]
+    lib = str(Path(torch.__file__).resolve().parent / "lib")
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    return includes, lib, abi
+
+
+def build(reference: Path = DEFAULT_REFERENCE, force: bool = False) -> Path:
+    sources = [reference / s for s in SOURCES]
+    missing = [str(s) for s in sources if not s.exists()]
+    if missing:
+        raise FileNotFoundError(f"reference sources not found: {missing}")
+    if OUT.exists() and not force and all(s.stat().st_mtime <= OUT.stat().st_mtime for s in sources):
+        return OUT
+    OUT_DIR.mkdir(parents=True, exist_ok=True)
+    includes, lib, abi = _torch_flags()
+    inc = [f"-I{p}" for p in includes] + [f"-I{reference / 'include'}"]
+    defs = [f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_EXTENSION_NAME=_C"]
+    objs = []
+    for src in sources:
+        obj = OUT_DIR / (src.name + ".o")
+        if src.suffix == ".cu":
+            cmd = ["/usr/local/cuda/bin/nvcc", "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17",
+                   "--expt-relaxed-constexpr", "-lineinfo", "-Xcompiler", "-fPIC", *defs, *inc, "-c", str(src),
+                   "-o", str(obj)]
+        else:
+            cmd = [os.environ.get("CXX", "g++"), "-O3", "-std=c++17", "-fPIC", *defs, *inc, "-c", str(src), "-o",
+                   str(obj)]
+        subprocess.run(cmd, check=True)
+        objs.append(str(obj))
+    tmp = OUT.with_suffix(".tmp.so")
+    subprocess.run(["/usr/local/cuda/bin/nvcc", "-gencode", "arch=compute_100a,code=sm_100a", "-shared", *objs,
+                    "-o", str(tmp), f"-L{lib}", "-lc10", "-lc10_cuda", "-ltorch_cpu", "-ltorch",
+                    f"-Xlinker=-rpath,{lib}"], check=True)
+    os.replace(tmp, OUT)
+    for obj in objs:
+        Path(obj).unlink(missing_ok=True)
+    return OUT
+
+
+def build_if_available() -> Path | None:
+    """Builds oracle/_ref/_C.so when the reference sources are present (this container); on the
+    GPU box the prebuilt library is used as shipped."""
+    if not DEFAULT_REFERENCE.exists():
+        return OUT if OUT.exists() else None
+    return build(DEFAULT_REFERENCE)
+
+
+def main() -> int:
+    parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    parser.add_argument("--reference", type=Path, default=DEFAULT_REFERENCE)
+    parser.add_argument("--force", action="store_true")
+    args = parser.parse_args()
+    print(build(args.reference, args.force))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -52,7 +52,7 @@ def parse_args(argv=None):
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--workload", choices=("decode", "verify", "copy", "stacked"), default="decode")
     p.add_argument("--e2e-steps", type=int, default=200)
-    p.add_argument("--decode-kernel", choices=("auto", "tmastore", "stream4", "stream2", "rowreg"), default="auto",
+    p.add_argument("--decode-kernel", choices=("auto", "stream", "rowreg", "tmastore", "staged1", "staged2", "staged4"), default="auto",
                    help="decode kernel variant (all compute the same results)")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline budget (rank 0, N=1)")
     p.add_argument("--no-cpu-baseline", action="store_true")

@@ -141,11 +141,13 @@ int ld_copy_slots(float* pool, int64_t n_pool_slots, int64_t pool_slot_stride,
                   int64_t slot_elems, void* stream);
 
 /* Decode kernel variants (ld_decode_kernel_override). */
-#define LD_DECODE_KERNEL_AUTO 0          /* library default: STREAM_4ROW for width 1, ROWREG otherwise */
-#define LD_DECODE_KERNEL_ROWREG 1        /* one CTA per (request, head), state loaded into registers */
-#define LD_DECODE_KERNEL_STREAM_4ROW 2   /* persistent TMA-bulk streaming kernel, 8 consumer warps */
-#define LD_DECODE_KERNEL_STREAM_2ROW 3   /* persistent TMA-bulk streaming kernel, 16 consumer warps */
-#define LD_DECODE_KERNEL_TMA_STORE 4     /* persistent kernel with TMA bulk loads and TMA bulk stores */
+#define LD_DECODE_KERNEL_AUTO 0        /* library default: STREAM for width-1 launches of >= 2 items per SM, else ROWREG */
+#define LD_DECODE_KERNEL_ROWREG 1      /* one CTA per (request, head), state loaded into registers */
+#define LD_DECODE_KERNEL_STREAM 2      /* persistent kernel: TMA bulk loads into a 3-deep ring, 8 consumer warps */
+#define LD_DECODE_KERNEL_TMA_STORE 3   /* persistent kernel with TMA bulk loads and TMA bulk stores */
+#define LD_DECODE_KERNEL_STAGED_Q1 4   /* one CTA per (request, head), TMA-staged state, 3 CTAs/SM */
+#define LD_DECODE_KERNEL_STAGED_Q2 5   /* two-CTA cluster per (request, head), 64 rows each */
+#define LD_DECODE_KERNEL_STAGED_Q4 6   /* four-CTA cluster per (request, head), 32 rows each */
 
 /*
  * Process-wide choice of the kernel that ld_decode launches, for tuning and for testing every

@@ -26,7 +26,7 @@ LD_FAULT_COPY_SLOT_RANGE = 0x10
 LD_FAULT_WAIT_TIMEOUT = 0x20
 HEAD_DIM = 128
 MAX_WIDTH = 4
-DECODE_KERNELS = {"auto": 0, "rowreg": 1, "stream4": 2, "stream2": 3, "tmastore": 4}
+DECODE_KERNELS = {"auto": 0, "rowreg": 1, "stream": 2, "tmastore": 3, "staged1": 4, "staged2": 5, "staged4": 6}
 
 _lib: ctypes.CDLL | None = None
 
@@ -91,8 +91,8 @@ def fault_flags(clear: bool = True) -> int:
 
 
 def set_decode_kernel(name: str) -> str:
-    """Select the kernel ld_decode launches ("auto", "rowreg", "stream4", "stream2"); returns the
-    previous selection.  All variants compute the same results."""
+    """Select the kernel ld_decode launches (a key of DECODE_KERNELS); returns the previous
+    selection.  All variants compute the same results."""
     previous = lib().ld_decode_kernel_override(DECODE_KERNELS[name])
     if previous < 0:
         raise LightDeltaError(-previous, last_error())

@@ -769,10 +769,10 @@ __device__ void consume(const DecodeArgs& p, Smem& sm, int tid) {
 }
 
 // Block: Tile<kRows>::kThreads consumer threads followed by one producer warp, one CTA per SM.
-// The register cap keeps the block launchable: warps are spread over the SM's four 16 K-register
-// sub-partitions, so 17 warps (2-row tile) allow 96 registers per thread and 9 warps allow 168.
+// The register cap keeps the block launchable: its 9 warps are spread over the SM's four 16 K-register
+// sub-partitions (at most 3 warps each), which allows 168 registers per thread.
 template <int kRows>
-__global__ void __maxnreg__(kRows == 2 ? 96 : 168) gdn_decode_stream_kernel(const DecodeArgs p) {
+__global__ void __maxnreg__(168) gdn_decode_stream_kernel(const DecodeArgs p) {
   constexpr int kConsumers = Tile<kRows>::kThreads;
   constexpr int kConsumerWarps = kConsumers / 32;
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -1055,6 +1055,258 @@ __global__ void __maxnreg__(168) gdn_decode_tmastore_kernel(const DecodeArgs p) 
 
 }  // namespace ts
 
+
+// ------------------------------------------------------------------------------------------
+// Staged kernel: one item split across a cluster of Q CTAs.  Each CTA owns 128/Q rows of the
+// (request, head) state, TMA-loads that row slice (64/Q KiB) and the item's activation rows into
+// shared memory, and runs the recurrence on a small register tile in row passes (rows are
+// independent until the output norm).  The gated RMSNorm needs all 128 outputs of a token: each
+// CTA reduces its rows' sum of squares and, for Q > 1, reads its peers' partial sums through
+// distributed shared memory.  Shared memory rather than registers holds the in-flight state, so
+// three CTAs per SM keep up to 192 KiB of loads in flight (Q = 1); Q = 2 or 4 spreads small
+// batches over more SMs.  Every CTA of a cluster takes the same path, so all reach its barriers.
+// ------------------------------------------------------------------------------------------
+namespace staged {
+
+constexpr int kThreads = 256;
+constexpr int kRowGroups = kThreads / kLanesPerRow;  // 32
+
+template <int Q>
+struct Shape {
+  static constexpr int kRowsPerCta = kDim / Q;                        // 128, 64, 32
+  static constexpr int kRowsPerThread = kRowsPerCta >= 64 ? 2 : 1;   // rows per thread per pass
+  static constexpr int kPasses = kRowsPerCta / (kRowGroups * kRowsPerThread);
+  static constexpr int kValuesPerLane = kRowsPerCta / 32;            // epilogue rows per lane
+};
+
+template <int Q>
+struct Smem {
+  float state[Shape<Q>::kRowsPerCta * kDim];
+  __nv_bfloat16 q[kMaxTokens][kDim];
+  __nv_bfloat16 k[kMaxTokens][kDim];
+  __nv_bfloat16 v[kMaxTokens][Shape<Q>::kRowsPerCta];
+  __nv_bfloat16 z[kMaxTokens][Shape<Q>::kRowsPerCta];
+  float o[kMaxTokens][Shape<Q>::kRowsPerCta];
+  float partial[kMaxTokens];
+  int dst[kMaxTokens];
+  float decay[kMaxTokens];
+  float beta[kMaxTokens];
+  int kind;
+  int n;
+  int bos;
+  unsigned long long full;
+};
+
+__device__ __forceinline__ unsigned int cluster_rank() {
+  unsigned int r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// Reads a float from the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ float peer_load(const float* local, unsigned int rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  float value;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(value) : "r"(remote) : "memory");
+  return value;
+}
+
+template <int Q>
+__device__ __forceinline__ void staged_body(const DecodeArgs& p, Smem<Q>& sm) {
+  using S = Shape<Q>;
+  constexpr int kRows = S::kRowsPerThread;
+  const int HV = p.num_v_heads;
+  const int W = p.width;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int j = tid & (kLanesPerRow - 1);
+  const int g = tid / kLanesPerRow;
+  const int64_t item = blockIdx.x / Q;
+  const unsigned int rank = Q > 1 ? cluster_rank() : 0u;
+  const int row0 = static_cast<int>(rank) * S::kRowsPerCta;
+  const int request = static_cast<int>(item / HV);
+  const int head = static_cast<int>(item - static_cast<int64_t>(request) * HV);
+
+  // Metadata (warp 0), then the TMA loads of this CTA's share of the item (thread 0).
+  if (warp == 0) {
+    const int bos = p.cu[request];
+    const int eos = p.cu[request + 1];
+    const int n = eos - bos;
+    int kind = kRun;
+    int src = 0;
+    if (n <= 0) {
+      kind = kSkip;
+    } else if (bos < 0 || static_cast<int64_t>(eos) > p.n_tokens) {
+      kind = kSkip;
+      if (lane == 0 && rank == 0) atomicOr(&g_decode_faults, LD_FAULT_DECODE_TOKENS);
+    } else {
+      const int acc = p.accepted[request];
+      src = (acc >= 1 && acc <= W) ? p.indices[request * W + acc - 1] : 0;
+      if (src <= 0 || n > W || src >= p.n_slots) {
+        kind = kZero;
+        if (lane == 0 && rank == 0) {
+          if (n > W) atomicOr(&g_decode_faults, LD_FAULT_DECODE_TOKENS);
+          if (src >= p.n_slots) atomicOr(&g_decode_faults, LD_FAULT_DECODE_SLOT_RANGE);
+        }
+      }
+    }
+    if (kind == kRun && lane < n) {
+      int dst = p.indices[request * W + lane];
+      if (dst >= p.n_slots) {
+        if (rank == 0) atomicOr(&g_decode_faults, LD_FAULT_DECODE_SLOT_RANGE);
+        dst = 0;
+      }
+      sm.dst[lane] = dst;
+      token_gates(p, bos + lane, head, sm.decay[lane], sm.beta[lane]);
+    }
+    if (lane == 0) {
+      sm.kind = kind;
+      sm.n = n;
+      sm.bos = bos;
+      mbar_init(&sm.full, 1);
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      if (kind == kRun) {
+        const int H = p.num_k_heads;
+        const int key_head = head / p.heads_ratio;
+        mbar_arrive_expect_tx(&sm.full, S::kRowsPerCta * kDim * 4 + n * (2 * kRowBytes + 4 * S::kRowsPerCta));
+        bulk_load(sm.state,
+                  p.state + static_cast<int64_t>(src) * p.slot_stride + static_cast<int64_t>(head) * kHeadElems +
+                      static_cast<int64_t>(row0) * kDim,
+                  S::kRowsPerCta * kDim * 4, &sm.full);
+        for (int t = 0; t < n; ++t) {
+          const int64_t token = bos + t;
+          const __nv_bfloat16* row = p.qkv + token * p.qkv_row;
+          bulk_load(sm.q[t], row + key_head * kDim, kRowBytes, &sm.full);
+          bulk_load(sm.k[t], row + (H + key_head) * kDim, kRowBytes, &sm.full);
+          bulk_load(sm.v[t], row + (2 * H + head) * kDim + row0, 2 * S::kRowsPerCta, &sm.full);
+          bulk_load(sm.z[t], p.gate + token * p.gate_row + head * kDim + row0, 2 * S::kRowsPerCta, &sm.full);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const int kind = sm.kind;
+  const int n = sm.n;
+  const int64_t bos = sm.bos;
+  if (kind == kSkip) return;  // the same for every CTA of the cluster
+  if (kind == kZero) {
+    for (int idx = tid; idx < n * S::kRowsPerCta; idx += kThreads) {
+      const int64_t token = bos + idx / S::kRowsPerCta;
+      p.out[(token * HV + head) * kDim + row0 + (idx % S::kRowsPerCta)] = __float2bfloat16_rn(0.0f);
+    }
+    return;
+  }
+  if (!mbar_wait(&sm.full, 0)) {
+    // The loads did not land in time: report, and keep the cluster's control flow intact.
+    if (tid == 0) atomicOr(&g_decode_faults, LD_FAULT_WAIT_TIMEOUT);
+  }
+
+  const int64_t head_offset = static_cast<int64_t>(head) * kHeadElems;
+#pragma unroll 1
+  for (int pass = 0; pass < S::kPasses; ++pass) {
+    const int pass_row = pass * kRowGroups * kRows;  // first local row of this pass
+    float4 tile[kRows][kVecPerRow];
+    {
+      const float4* src4 = reinterpret_cast<const float4*>(sm.state + (pass_row + g) * kDim + 4 * j);
+#pragma unroll
+      for (int i = 0; i < kRows; ++i) {
+#pragma unroll
+        for (int c = 0; c < kVecPerRow; ++c) tile[i][c] = src4[(i * kRowGroups * kDim + c * 4 * kLanesPerRow) / 4];
+      }
+    }
+    for (int t = 0; t < n; ++t) {
+      float4 kv[kVecPerRow], qv[kVecPerRow];
+      float k_sq, q_sq;
+      load_row_cols(sm.k[t], j, kv, k_sq);
+      load_row_cols(sm.q[t], j, qv, q_sq);
+      k_sq = row_sum(k_sq);
+      q_sq = row_sum(q_sq);
+      // L2 norm in fp32 as gdn.py:98-99; q then scaled by K^-1/2 as gdn.py:101.
+      const float k_inv = 1.0f / sqrtf(k_sq + 1e-6f);
+      const float q_inv = 1.0f / sqrtf(q_sq + 1e-6f);
+#pragma unroll
+      for (int c = 0; c < kVecPerRow; ++c) {
+        kv[c] = make_float4(kv[c].x * k_inv, kv[c].y * k_inv, kv[c].z * k_inv, kv[c].w * k_inv);
+        qv[c] = make_float4(qv[c].x * q_inv * p.q_scale, qv[c].y * q_inv * p.q_scale, qv[c].z * q_inv * p.q_scale,
+                            qv[c].w * q_inv * p.q_scale);
+      }
+      float vrow[kRows], o[kRows];
+#pragma unroll
+      for (int i = 0; i < kRows; ++i) vrow[i] = __bfloat162float(sm.v[t][pass_row + g + i * kRowGroups]);
+      tile_step<kRows>(tile, kv, qv, vrow, sm.decay[t], sm.beta[t], o);
+      if (j == 0) {
+#pragma unroll
+        for (int i = 0; i < kRows; ++i) {
+          // The recurrence output is rounded to bf16 before the norm (gdn.py:116).
+          sm.o[t][pass_row + g + i * kRowGroups] = __bfloat162float(__float2bfloat16_rn(o[i]));
+        }
+      }
+      const int dst = sm.dst[t];
+      if (dst > 0) {
+        float4* out4 = reinterpret_cast<float4*>(p.state + static_cast<int64_t>(dst) * p.slot_stride + head_offset +
+                                                 static_cast<int64_t>(row0 + pass_row + g) * kDim + 4 * j);
+#pragma unroll
+        for (int i = 0; i < kRows; ++i) {
+#pragma unroll
+          for (int c = 0; c < kVecPerRow; ++c) out4[(i * kRowGroups * kDim + c * 4 * kLanesPerRow) / 4] = tile[i][c];
+        }
+      }
+    }
+  }
+  __syncthreads();  // every local row's output is in sm.o
+
+  // Gated RMSNorm (gdn.py:117-119): warp t normalises token t over all 128 rows of the head.
+  constexpr int E = S::kValuesPerLane;
+  float ov[E];
+  float sq = 0.0f;  // after warp_sum: this CTA's sum of squares of token `warp`, in every lane
+  if (warp < n) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      ov[e] = sm.o[warp][E * lane + e];
+      sq += ov[e] * ov[e];
+    }
+    sq = warp_sum(sq);
+    if (Q > 1 && lane == 0) sm.partial[warp] = sq;
+  }
+  if constexpr (Q > 1) cluster_sync();  // every CTA's partial sums are visible cluster-wide
+  if (warp < n) {
+    float total = sq;
+    if constexpr (Q > 1) {
+      // Summed in rank order by every CTA of the cluster, so all of them use the same value.
+      total = 0.0f;
+#pragma unroll
+      for (int r = 0; r < Q; ++r) total += peer_load(&sm.partial[warp], r);
+    }
+    const float rstd = 1.0f / sqrtf(total / static_cast<float>(kDim) + p.eps);
+    const int64_t token = bos + warp;
+    __nv_bfloat16* out_row = p.out + (token * HV + head) * kDim + row0 + E * lane;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const int row = row0 + E * lane + e;
+      const float z = __bfloat162float(sm.z[warp][E * lane + e]);
+      const float silu = z / (1.0f + expf(-z));
+      const float w = load_param(p.weight, row, p.weight_bf16);
+      out_row[e] = __float2bfloat16_rn(ov[e] * rstd * w * silu);
+    }
+  }
+  if constexpr (Q > 1) cluster_sync();  // no CTA leaves while a peer may still read its partials
+}
+
+template <int Q>
+__global__ void __cluster_dims__(Q, 1, 1) __launch_bounds__(kThreads, 3) gdn_decode_staged_kernel(const DecodeArgs p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  staged_body<Q>(p, *reinterpret_cast<Smem<Q>*>(smem_raw));
+}
+
+}  // namespace staged
+
 }  // namespace stream
 
 bool aligned(const void* ptr, uintptr_t bytes) { return (reinterpret_cast<uintptr_t>(ptr) % bytes) == 0; }
@@ -1079,17 +1331,30 @@ int device_info(DeviceInfo& out) {
   if (!info.stream_ready) {
     err = cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, device);
     if (err != cudaSuccess) return set_error(LD_ERR_CUDA, "SM count: %s", cudaGetErrorString(err));
-    for (auto kernel : {stream::gdn_decode_stream_kernel<4>, stream::gdn_decode_stream_kernel<2>}) {
-      err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(sizeof(stream::Smem)));
-      if (err != cudaSuccess) return set_error(LD_ERR_CUDA, "shared-memory opt-in: %s", cudaGetErrorString(err));
-    }
+    err = cudaFuncSetAttribute(stream::gdn_decode_stream_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(sizeof(stream::Smem)));
+    if (err != cudaSuccess) return set_error(LD_ERR_CUDA, "shared-memory opt-in: %s", cudaGetErrorString(err));
     err = cudaFuncSetAttribute(stream::ts::gdn_decode_tmastore_kernel<2, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(sizeof(stream::ts::Smem<2, 1>)));
     if (err == cudaSuccess) {
       err = cudaFuncSetAttribute(stream::ts::gdn_decode_tmastore_kernel<1, 2>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(sizeof(stream::ts::Smem<1, 2>)));
+    }
+    if (err == cudaSuccess) {
+      err = cudaFuncSetAttribute(stream::staged::gdn_decode_staged_kernel<1>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(sizeof(stream::staged::Smem<1>)));
+    }
+    if (err == cudaSuccess) {
+      err = cudaFuncSetAttribute(stream::staged::gdn_decode_staged_kernel<2>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(sizeof(stream::staged::Smem<2>)));
+    }
+    if (err == cudaSuccess) {
+      err = cudaFuncSetAttribute(stream::staged::gdn_decode_staged_kernel<4>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(sizeof(stream::staged::Smem<4>)));
     }
     if (err != cudaSuccess) return set_error(LD_ERR_CUDA, "shared-memory opt-in: %s", cudaGetErrorString(err));
     info.stream_ready = true;
@@ -1148,8 +1413,8 @@ extern "C" int ld_decode(const void* qkv, int64_t qkv_row_stride, const void* a,
     return set_error(LD_ERR_INVALID, "dt_bias and weight must be FP32 or BF16");
   }
   if (n_requests == 0) return ok();
-  if (n_requests * num_v_heads > 0x7fffffffLL) {
-    return set_error(LD_ERR_INVALID, "n_requests * num_v_heads exceeds the grid limit");
+  if (4 * n_requests * num_v_heads > 0x7fffffffLL) {
+    return set_error(LD_ERR_INVALID, "4 * n_requests * num_v_heads exceeds the grid limit");
   }
   if (qkv == nullptr || a == nullptr || b == nullptr || a_log == nullptr || dt_bias == nullptr ||
       indices == nullptr || cu == nullptr || accepted == nullptr || state == nullptr ||
@@ -1204,21 +1469,30 @@ extern "C" int ld_decode(const void* qkv, int64_t qkv_row_stride, const void* a,
   // TMA bulk copies need 16-byte aligned sources: qkv and gate rows must start on 16 bytes.
   const bool bulk_ok = aligned(qkv, 16) && qkv_row_stride % 8 == 0 && aligned(gate, 16) &&
                        gate_row_stride % 8 == 0 && aligned(out, 8);
-  int variant = g_kernel_override.load(std::memory_order_relaxed);
-  if (variant == LD_DECODE_KERNEL_AUTO) {
-    // Measured on B200 (BASELINE configs 2 and 3): the streaming kernel is fastest for one-token
-    // decode, the one-CTA-per-item kernel for multi-token verify, whose four state writes per
-    // item favour its two resident CTAs per SM.
-    variant = width == 1 ? LD_DECODE_KERNEL_STREAM_4ROW : LD_DECODE_KERNEL_ROWREG;
-  }
-  if (!bulk_ok) variant = LD_DECODE_KERNEL_ROWREG;
+  int variant = bulk_ok ? g_kernel_override.load(std::memory_order_relaxed) : LD_DECODE_KERNEL_ROWREG;
+  DeviceInfo info;
   if (variant != LD_DECODE_KERNEL_ROWREG) {
-    DeviceInfo info;
     const int rc = device_info(info);
     if (rc != LD_OK) return rc;
+  }
+  if (variant == LD_DECODE_KERNEL_AUTO) {
+    // Measured on B200 (BASELINE configs 2 and 3, HV=48 batches 1..32): the streaming kernel is
+    // fastest for one-token decode once there are at least two items per SM; the one-CTA-per-item
+    // kernel wins for smaller launches and for multi-token verify, whose four state writes per
+    // item favour its two resident CTAs per SM.
+    variant = (width == 1 && args.total_items >= 2 * info.sms) ? LD_DECODE_KERNEL_STREAM : LD_DECODE_KERNEL_ROWREG;
+  }
+  if (variant != LD_DECODE_KERNEL_ROWREG) {
     const unsigned int grid = static_cast<unsigned int>(std::min<int64_t>(args.total_items, info.sms));
-    if (variant == LD_DECODE_KERNEL_STREAM_2ROW) {
-      stream::gdn_decode_stream_kernel<2><<<grid, Tile<2>::kThreads + 32, sizeof(stream::Smem), s>>>(args);
+    if (variant == LD_DECODE_KERNEL_STAGED_Q1) {
+      stream::staged::gdn_decode_staged_kernel<1>
+          <<<static_cast<unsigned int>(args.total_items), stream::staged::kThreads, sizeof(stream::staged::Smem<1>), s>>>(args);
+    } else if (variant == LD_DECODE_KERNEL_STAGED_Q2) {
+      stream::staged::gdn_decode_staged_kernel<2><<<static_cast<unsigned int>(2 * args.total_items),
+                                                    stream::staged::kThreads, sizeof(stream::staged::Smem<2>), s>>>(args);
+    } else if (variant == LD_DECODE_KERNEL_STAGED_Q4) {
+      stream::staged::gdn_decode_staged_kernel<4><<<static_cast<unsigned int>(4 * args.total_items),
+                                                    stream::staged::kThreads, sizeof(stream::staged::Smem<4>), s>>>(args);
     } else if (variant == LD_DECODE_KERNEL_TMA_STORE) {
       if (width == 1) {
         stream::ts::gdn_decode_tmastore_kernel<2, 1><<<grid, stream::ts::kThreads, sizeof(stream::ts::Smem<2, 1>), s>>>(
@@ -1248,7 +1522,7 @@ extern "C" int ld_decode(const void* qkv, int64_t qkv_row_stride, const void* a,
 }
 
 extern "C" int ld_decode_kernel_override(int variant) {
-  if (variant < LD_DECODE_KERNEL_AUTO || variant > LD_DECODE_KERNEL_TMA_STORE) {
+  if (variant < LD_DECODE_KERNEL_AUTO || variant > LD_DECODE_KERNEL_STAGED_Q4) {
     return ldb::set_error(-LD_ERR_INVALID, "unknown decode kernel variant %d", variant);
   }
   return ldb::g_kernel_override.exchange(variant);

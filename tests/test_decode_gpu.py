@@ -21,7 +21,7 @@ from lightdelta_b200.config import BackendConfig
 
 pytestmark = pytest.mark.gpu
 
-VARIANTS = ["tmastore", "stream4", "stream2", "rowreg"]
+VARIANTS = ["auto", "stream", "rowreg", "tmastore", "staged1", "staged2", "staged4"]
 
 
 @pytest.fixture(params=VARIANTS)

@@ -1,0 +1,44 @@
+"""CPU checks of bench.py: argument rules and the reference arm's JSON line (which runs the
+CPU oracle port and needs no GPU)."""
+
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+sys.path.insert(0, str(ROOT))
+
+import bench  # noqa: E402
+
+
+def test_warmup_below_three_is_rejected():
+    with pytest.raises(SystemExit):
+        bench.parse_args(["--warmup", "2"])
+
+
+def test_defaults_are_the_headline_workload():
+    args = bench.parse_args([])
+    assert (args.gpus, args.workload, args.impl, args.decode_kernel) == (1, "decode", "ours", "auto")
+    assert args.warmup >= 3
+
+
+def test_reference_arm_prints_one_contract_line():
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    result = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "3",
+                             "--warmup", "3"], capture_output=True, text=True, timeout=600, env=env, check=True)
+    lines = [line for line in result.stdout.splitlines() if line.strip()]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "scaling", "vs_baseline", "dtype", "data", "config", "impl", "cpu_baseline", "e2e"):
+        assert key in line, key
+    assert line["impl"] == "reference" and line["unit"] == "tokens/s" and line["value"] > 0
+    assert line["metric"] == bench.METRIC
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+    assert line["e2e"] == {"value": line["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                           "d2h_bytes_per_step": 0}
+    assert line["config"]["workload"] == "config2_decode"

@@ -6,6 +6,7 @@
 Workloads (the default is the one the headline metric is quoted on):
   decode  config 2: indexed decode, 256 sequences per GPU, T=1, pool of 1024 fp32 slots [32,128,128]
   verify  config 3: MTP verify, 64 sequences per GPU, T=4, accepted ~ U{1..4}
+  commit  config 3's explicit commit: copy_state of each sequence's accepted slot to its home slot
   copy    config 4: gather 512 slots of a 2048-slot layer pool, scatter them to a permuted set
   stacked config 5: 48 layers of T=4 verify over 2048 sequences sharded across the ranks (strong
           scaling), replayed as one CUDA graph per step; run it with a few --steps (~0.2 s each)
@@ -50,7 +51,7 @@ def parse_args(argv=None):
     p.add_argument("--steps", type=int, default=4000)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--workload", choices=("decode", "verify", "copy", "stacked"), default="decode")
+    p.add_argument("--workload", choices=("decode", "verify", "commit", "copy", "stacked"), default="decode")
     p.add_argument("--e2e-steps", type=int, default=200)
     p.add_argument("--decode-kernel", choices=("auto", "stream", "rowreg", "tmastore", "staged1", "staged2", "staged4"), default="auto",
                    help="decode kernel variant (all compute the same results)")
@@ -241,6 +242,25 @@ def run_ours(args, dist: Dist) -> dict | None:
                   "sequences_per_gpu": requests, "tokens_per_sequence": width, "num_k_heads": h,
                   "num_v_heads": hv, "head_dim": 128, "pool_slots": case.pool.shape[0],
                   "state_dtype": "fp32", "activation_dtype": "bf16", "decode_kernel": args.decode_kernel}
+    elif args.workload == "commit":
+        # Config 3's explicit commit: after verify, copy each sequence's accepted step state to
+        # its home slot (the first of its candidate slots) with the pool-to-pool copy op.
+        verify = workloads.config3(device, seed=3 + seed)
+        pool = verify.pool
+        src = verify.slots.gather(1, (verify.accepted - 1).long()[:, None]).flatten().contiguous()
+        dst = verify.slots[:, 0].contiguous()
+
+        def fn():
+            torch.ops.lightdelta.copy_state(pool, src, dst)
+
+        moved = int((src != dst).sum().item())
+        bytes_per_launch = moved * 2 * verify.num_v_heads * workloads.SLOT_HEAD_BYTES
+        touched = bytes_per_launch
+        units_per_step, unit = verify.slots.shape[0], "sequences/s"
+        case = None
+        config = {"workload": "config3_commit_copy", "sequences_per_gpu": verify.slots.shape[0],
+                  "slots_copied_per_step": moved, "pool_slots": pool.shape[0],
+                  "note": "a sequence whose accepted slot is its home slot copies nothing"}
     elif args.workload == "stacked":
         from lightdelta_b200 import sharding
 
@@ -323,7 +343,7 @@ def run_ours(args, dist: Dist) -> dict | None:
         "higher_is_better": True,
         "scaling": "strong" if args.workload == "stacked" else "weak",
         "vs_baseline": None,
-        "dtype": "fp32" if args.workload != "copy" else "fp32 (bit copy)",
+        "dtype": "fp32 (bit copy)" if args.workload in ("copy", "commit") else "fp32",
         "data": "synthetic (seeded, BASELINE config shapes and distributions)",
         "impl": "ours",
         "config": {**config, "parallelism": f"slot-sharded x{dist.world}, no collective",

@@ -7,6 +7,8 @@ Workloads (the default is the one the headline metric is quote
   decode  config 2: indexed decode, 256 sequences per GPU, T=1, pool of 1024 fp32 slots [32,128,128]
   verify  config 3: MTP verify, 64 sequences per GPU, T=4, accepted ~ U{1..4}
   commit  config 3's explicit commit: copy_state of each sequence's accepted slot to its home slot
+  sample  config 3's greedy draft verification (greedy_verify): 64 requests x 3 drafts, 4 fp32
+          logits rows each over a 151,936-token vocabulary
   copy    config 4: gather 512 slots of a 2048-slot layer pool, scatter them to a permuted set
   stacked config 5: 48 layers of T=4 verify over 2048 sequences sharded across the ranks (strong
           scaling), replayed as one CUDA graph per step; run it with a few --steps (~0.2 s each)
@@ -51,7 +53,8 @@ def parse_args(argv=None):
     p.add_argument("--steps", type=int, default=4000)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--workload", choices=("decode", "verify", "commit", "copy", "stacked"), default="decode")
+    p.add_argument("--workload", choices=("decode", "verify", "commit", "sample", "copy", "stacked"),
+                   default="decode")
     p.add_argument("--e2e-steps", type=int, default=200)
     p.add_argument("--decode-kernel", choices=("auto", "stream", "rowreg", "tmastore", "staged1", "staged2", "staged4"), default="auto",
                    help="decode kernel variant (all compute the same results)")
@@ -245,22 +248,49 @@ def run_ours(args, dist: Dist) -> dict | None:
     elif args.workload == "commit":
         # Config 3's explicit commit: after verify, copy each sequence's accepted step state to
         # its home slot (the first of its candidate slots) with the pool-to-pool copy op.
-        verify = workloads.config3(device, seed=3 + seed)
-        pool = verify.pool
-        src = verify.slots.gather(1, (verify.accepted - 1).long()[:, None]).flatten().contiguous()
-        dst = verify.slots[:, 0].contiguous()
+        # Four independent config-3 batches on one 1025-slot pool, used in turn, so that the
+        # slots one step reads were last touched four steps earlier (> 126 MB L2 in between).
+        first = workloads.config3(device, seed=3 + seed, pool_slots=1025)
+        pool = first.pool
+        sets = []
+        for k in range(4):
+            verify = first if k == 0 else workloads.config3(device, seed=3 + seed + 17 * k, pool_slots=1025,
+                                                            pool=pool)
+            src = verify.slots.gather(1, (verify.accepted - 1).long()[:, None]).flatten().contiguous()
+            sets.append((src, verify.slots[:, 0].contiguous()))
+        turn = [0]
 
         def fn():
+            src, dst = sets[turn[0] % 4]
+            turn[0] += 1
             torch.ops.lightdelta.copy_state(pool, src, dst)
 
-        moved = int((src != dst).sum().item())
-        bytes_per_launch = moved * 2 * verify.num_v_heads * workloads.SLOT_HEAD_BYTES
-        touched = bytes_per_launch
-        units_per_step, unit = verify.slots.shape[0], "sequences/s"
+        moved_per_set = [int((src != dst).sum().item()) for src, dst in sets]
+        moved = sum(moved_per_set) / 4
+        bytes_per_launch = moved * 2 * first.num_v_heads * workloads.SLOT_HEAD_BYTES
+        touched = sum(moved_per_set) * 2 * first.num_v_heads * workloads.SLOT_HEAD_BYTES
+        units_per_step, unit = first.slots.shape[0], "sequences/s"
         case = None
-        config = {"workload": "config3_commit_copy", "sequences_per_gpu": verify.slots.shape[0],
-                  "slots_copied_per_step": moved, "pool_slots": pool.shape[0],
+        config = {"workload": "config3_commit_copy", "sequences_per_gpu": first.slots.shape[0],
+                  "slots_copied_per_step": moved, "pool_slots": pool.shape[0], "batches_in_turn": 4,
                   "note": "a sequence whose accepted slot is its home slot copies nothing"}
+    elif args.workload == "sample":
+        sampling = workloads.sampling_case(device, seed=6 + seed)
+        turn = [0]
+
+        def fn():
+            buffer = turn[0] % len(sampling.logits)
+            turn[0] += 1
+            torch.ops.lightdelta.greedy_verify(*sampling.op_args(buffer))
+
+        bytes_per_launch = sampling.bytes_per_launch()
+        touched = bytes_per_launch * len(sampling.logits)
+        units_per_step, unit = sampling.requests, "requests/s"
+        case = None
+        rows, vocab = sampling.logits[0].shape
+        config = {"workload": "config3_greedy_verify", "requests_per_gpu": sampling.requests,
+                  "draft_tokens": sampling.sampled.shape[1] - 1, "logits_rows": rows, "vocab": vocab,
+                  "logits_dtype": "fp32", "logits_buffers_in_turn": len(sampling.logits)}
     elif args.workload == "stacked":
         from lightdelta_b200 import sharding
 
@@ -328,6 +358,8 @@ def run_ours(args, dist: Dist) -> dict | None:
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline and args.workload in ("decode", "verify"):
         cpu = cpu_baseline(case, args.cpu_seconds)
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline and args.workload == "sample":
+        cpu = sampling_cpu_baseline(sampling, args.cpu_seconds)
 
     if dist.rank != 0:
         return None
@@ -343,7 +375,8 @@ def run_ours(args, dist: Dist) -> dict | None:
         "higher_is_better": True,
         "scaling": "strong" if args.workload == "stacked" else "weak",
         "vs_baseline": None,
-        "dtype": "fp32 (bit copy)" if args.workload in ("copy", "commit") else "fp32",
+        "dtype": {"copy": "fp32 (bit copy)", "commit": "fp32 (bit copy)",
+                  "sample": "fp32 logits, int32 tokens"}.get(args.workload, "fp32"),
         "data": "synthetic (seeded, BASELINE config shapes and distributions)",
         "impl": "ours",
         "config": {**config, "parallelism": f"slot-sharded x{dist.world}, no collective",
@@ -521,6 +554,33 @@ def cpu_baseline(case, seconds: float) -> dict:
     return {"value": w["tokens"] * reps / elapsed, "unit": "tokens/s", "cores": w["threads"], "kind": "port",
             "sample": f"full batch ({w['requests']} sequences, {w['tokens']} tokens) x {reps} repetitions, "
                       f"{elapsed:.1f} s, C oracle with OpenMP"}
+
+
+def sampling_cpu_baseline(sampling, seconds: float) -> dict:
+    """The C oracle of greedy verification on one logits buffer, repeated for ~`seconds`."""
+    import oracle
+
+    host = {k: getattr(sampling, k).cpu().numpy() for k in
+            ("cu_num_logits", "query_start_loc", "input_ids", "num_draft_tokens", "seq_lens", "prefill_len")}
+    logits = sampling.logits[0].float().cpu().numpy()
+    steps = sampling.sampled.shape[1] - 1
+    threads = oracle.default_threads()
+
+    def step():
+        oracle.greedy_verify(logits, host["cu_num_logits"], host["query_start_loc"], host["input_ids"],
+                             host["num_draft_tokens"], host["seq_lens"], host["prefill_len"], steps, threads)
+
+    step()
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        step()
+        reps += 1
+        elapsed = time.perf_counter() - t0
+        if elapsed >= seconds:
+            break
+    return {"value": sampling.requests * reps / elapsed, "unit": "requests/s", "cores": threads, "kind": "port",
+            "sample": f"one {logits.shape[0]}x{logits.shape[1]} fp32 logits batch x {reps} repetitions, "
+                      f"{elapsed:.1f} s, C oracle (argmax + prefix check) with OpenMP"}
 
 
 def run_reference(args, dist: Dist) -> dict | None:

@@ -35,6 +35,9 @@ extern "C" {
 /* Element types of the dtype-polymorphic parameters (dt_bias, norm weight). */
 #define LD_DTYPE_F32 0
 #define LD_DTYPE_BF16 1
+#define LD_DTYPE_F16 2 /* ld_greedy_verify logits only */
+#define LD_DTYPE_I32 3 /* token ids */
+#define LD_DTYPE_I64 4 /* token ids */
 
 /* Bits of the device fault word (ld_fault_flags). */
 #define LD_FAULT_DECODE_SLOT_RANGE 0x1u   /* decode: a slot index >= n_slots */
@@ -43,12 +46,17 @@ extern "C" {
 #define LD_FAULT_SCATTER_SLOT_RANGE 0x8u  /* scatter_state: a slot index >= n_pool_slots */
 #define LD_FAULT_COPY_SLOT_RANGE 0x10u    /* copy_slots: a slot index >= n_pool_slots */
 #define LD_FAULT_WAIT_TIMEOUT 0x20u       /* a bounded in-kernel wait expired; that launch's results are incomplete */
+#define LD_FAULT_VERIFY_DRAFTS 0x40u      /* greedy_verify: a request has more drafts than steps */
+#define LD_FAULT_VERIFY_RANGE 0x80u       /* greedy_verify: metadata points outside the logits or token ids */
 
 /* Head dimension handled by every kernel (K = V). */
 #define LD_HEAD_DIM 128
 /* Largest number of tokens per request (MTP verify window), csrc/register.cpp:5-7 schema
  * limit enforced at csrc/gdn_decode.cu:394-395. */
 #define LD_MAX_WIDTH 4
+/* Largest number of draft tokens per request in ld_greedy_verify (its sampled rows hold
+ * num_speculative_steps + 1 tokens). */
+#define LD_MAX_VERIFY_STEPS 7
 
 /* Message of the last LD_ERR_* returned on the calling thread ("" if none). */
 const char* ld_last_error(void);
@@ -163,6 +171,47 @@ int ld_decode_kernel_override(int variant);
  * This call synchronises the device; it is a diagnostic, not part of the hot path.
  */
 int ld_fault_flags(uint32_t* flags, int clear);
+
+/*
+ * Greedy MTP verification (the device form of the reference's rejection sampler,
+ * python/lightdelta/runtime/speculation.py:274-326, LightDeltaRejectionSampler.__call__):
+ *
+ *   target = argmax over each logits row (first index of the maximum; NaN counts as the maximum)
+ *   for each request r, with begin = cu_num_logits[r], end = cu_num_logits[r+1],
+ *   d = num_draft_tokens[r] and drafts = input_ids[query_start_loc[r+1]-d, query_start_loc[r+1]):
+ *     d == 0: sampled[r,0] = target[begin]; num_sampled[r] = 1 (0 for a prefill row)
+ *     else:   accepted = length of the prefix with begin+i < end and target[begin+i] == drafts[i];
+ *             sampled[r, 0..accepted) = drafts, sampled[r, accepted] = target[min(begin+accepted, end-1)];
+ *             num_sampled[r] = accepted + 1 and num_rejected[r] = (end - begin) - (accepted + 1),
+ *             both 0 for a prefill row (seq_lens[r] < prefill_len[r]).
+ *   The remaining entries of sampled[r, 0..num_speculative_steps] are -1; num_rejected is 0
+ *   where not set above.
+ *
+ * logits: [n_logits, vocab] of logits_dtype (F32, BF16 or F16), unit inner stride,
+ *   logits_row_stride elements between rows.  Only the rows a request consults are read.
+ * cu_num_logits, query_start_loc: int32 [n_requests + 1]; num_draft_tokens, seq_lens,
+ *   prefill_len: int32 [n_requests].
+ * input_ids: [n_input_ids] of token_dtype (I32 or I64); sampled: [n_requests,
+ *   num_speculative_steps + 1] of token_dtype, row-major; num_sampled, num_rejected: int32
+ *   [n_requests].  Every output entry is written.
+ * Where the reference raises (d > num_speculative_steps) or indexes outside the logits or
+ * input_ids, the request's row is -1 / 0 / 0 and LD_FAULT_VERIFY_DRAFTS or
+ * LD_FAULT_VERIFY_RANGE is set in the fault word.
+ * 0 <= num_speculative_steps <= LD_MAX_VERIFY_STEPS.
+ */
+int ld_greedy_verify(const void* logits, int logits_dtype, int64_t n_logits, int64_t vocab,
+                     int64_t logits_row_stride, const int32_t* cu_num_logits, const int32_t* query_start_loc,
+                     const void* input_ids, int token_dtype, int64_t n_input_ids, const int32_t* num_draft_tokens,
+                     const int32_t* seq_lens, const int32_t* prefill_len, int64_t n_requests,
+                     int64_t num_speculative_steps, void* sampled, int32_t* num_sampled, int32_t* num_rejected,
+                     void* stream);
+
+/*
+ * Process-wide thread-block cluster size of ld_greedy_verify (0 = automatic, or 1, 2, 4, 8, 16
+ * CTAs per request), for tuning and tests; results do not depend on it.  Returns the previous
+ * setting, or -LD_ERR_INVALID for another value.  No counterpart in the reference.
+ */
+int ld_greedy_verify_cluster_override(int cluster);
 
 #ifdef __cplusplus
 }

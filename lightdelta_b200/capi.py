@@ -18,14 +18,20 @@ LD_ERR_INVALID = 1
 LD_ERR_CUDA = 2
 LD_DTYPE_F32 = 0
 LD_DTYPE_BF16 = 1
+LD_DTYPE_F16 = 2
+LD_DTYPE_I32 = 3
+LD_DTYPE_I64 = 4
 LD_FAULT_DECODE_SLOT_RANGE = 0x1
 LD_FAULT_DECODE_TOKENS = 0x2
 LD_FAULT_GATHER_SLOT_RANGE = 0x4
 LD_FAULT_SCATTER_SLOT_RANGE = 0x8
 LD_FAULT_COPY_SLOT_RANGE = 0x10
 LD_FAULT_WAIT_TIMEOUT = 0x20
+LD_FAULT_VERIFY_DRAFTS = 0x40
+LD_FAULT_VERIFY_RANGE = 0x80
 HEAD_DIM = 128
 MAX_WIDTH = 4
+MAX_VERIFY_STEPS = 7
 DECODE_KERNELS = {"auto": 0, "rowreg": 1, "stream": 2, "tmastore": 3, "staged1": 4, "staged2": 5, "staged4": 6}
 
 _lib: ctypes.CDLL | None = None
@@ -66,6 +72,10 @@ def lib() -> ctypes.CDLL:
     handle.ld_fault_flags.restype = i32
     handle.ld_decode_kernel_override.argtypes = [i32]
     handle.ld_decode_kernel_override.restype = i32
+    handle.ld_greedy_verify.argtypes = [p, i32, i64, i64, i64, p, p, p, i32, i64, p, p, p, i64, i64, p, p, p, p]
+    handle.ld_greedy_verify.restype = i32
+    handle.ld_greedy_verify_cluster_override.argtypes = [i32]
+    handle.ld_greedy_verify_cluster_override.restype = i32
     _lib = handle
     return handle
 
@@ -97,6 +107,15 @@ def set_decode_kernel(name: str) -> str:
     if previous < 0:
         raise LightDeltaError(-previous, last_error())
     return {v: k for k, v in DECODE_KERNELS.items()}[previous]
+
+
+def set_verify_cluster(cluster: int) -> int:
+    """Force ld_greedy_verify's cluster size (1, 2, 4 or 8 CTAs per request; 0 = automatic);
+    returns the previous setting.  Results do not depend on it."""
+    previous = lib().ld_greedy_verify_cluster_override(int(cluster))
+    if previous < 0:
+        raise LightDeltaError(-previous, last_error())
+    return previous
 
 
 # ---------------------------------------------------------------------------------------------
@@ -158,4 +177,20 @@ def copy_slots(pool, src, dst, stream=None):
     check(lib().ld_copy_slots(
         pool.data_ptr(), pool.shape[0], pool.stride(0), src.data_ptr(), src.stride(0), dst.data_ptr(),
         dst.stride(0), src.numel(), _slot_elems(pool), _stream(pool, stream),
+    ))
+
+
+def greedy_verify(logits, cu_num_logits, query_start_loc, input_ids, num_draft_tokens, seq_lens, prefill_len,
+                  sampled, num_sampled, num_rejected, stream=None):
+    """ld_greedy_verify on torch tensors laid out as torch.ops.lightdelta.greedy_verify expects."""
+    import torch
+
+    logits_code = {torch.float32: LD_DTYPE_F32, torch.bfloat16: LD_DTYPE_BF16, torch.float16: LD_DTYPE_F16}
+    token_code = {torch.int32: LD_DTYPE_I32, torch.int64: LD_DTYPE_I64}
+    check(lib().ld_greedy_verify(
+        logits.data_ptr(), logits_code[logits.dtype], logits.shape[0], logits.shape[1], logits.stride(0),
+        cu_num_logits.data_ptr(), query_start_loc.data_ptr(), input_ids.data_ptr(), token_code[input_ids.dtype],
+        input_ids.numel(), num_draft_tokens.data_ptr(), seq_lens.data_ptr(), prefill_len.data_ptr(),
+        num_draft_tokens.numel(), sampled.shape[1] - 1, sampled.data_ptr(), num_sampled.data_ptr(),
+        num_rejected.data_ptr(), _stream(logits, stream),
     ))

@@ -36,11 +36,13 @@ extern "C" const char* ld_version(void) { return "lightdelta_b200 0.1.0 (sm_100a
 
 extern "C" int ld_fault_flags(uint32_t* flags, int clear) {
   if (flags == nullptr) return ldb::set_error(LD_ERR_INVALID, "ld_fault_flags: flags is NULL");
-  uint32_t decode = 0, state_io = 0;
+  uint32_t decode = 0, state_io = 0, verify = 0;
   int rc = ldb::decode_faults(&decode, clear);
   if (rc != LD_OK) return rc;
   rc = ldb::state_io_faults(&state_io, clear);
   if (rc != LD_OK) return rc;
-  *flags = decode | state_io;
+  rc = ldb::verify_faults(&verify, clear);
+  if (rc != LD_OK) return rc;
+  *flags = decode | state_io | verify;
   return ldb::ok();
 }

@@ -13,5 +13,6 @@ int ok();
 // Per-translation-unit device fault words (see LD_FAULT_* in lightdelta_b200.h).
 int decode_faults(uint32_t* flags, int clear);
 int state_io_faults(uint32_t* flags, int clear);
+int verify_faults(uint32_t* flags, int clear);
 
 }  // namespace ldb

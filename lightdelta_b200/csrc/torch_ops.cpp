@@ -136,6 +136,49 @@ void copy_state(at::Tensor pool, const at::Tensor& src, const at::Tensor& dst) {
                          stream_of(pool)));
 }
 
+// Extension (no reference schema): the device form of LightDeltaRejectionSampler.__call__
+// (python/lightdelta/runtime/speculation.py:274-326), writing every entry of its three outputs.
+void greedy_verify(const at::Tensor& logits, const at::Tensor& cu_num_logits, const at::Tensor& query_start_loc,
+                   const at::Tensor& input_ids, const at::Tensor& num_draft_tokens, const at::Tensor& seq_lens,
+                   const at::Tensor& prefill_len, at::Tensor sampled, at::Tensor num_sampled,
+                   at::Tensor num_rejected) {
+  TORCH_CHECK(logits.is_cuda() && logits.dim() == 2 && logits.stride(1) == 1 &&
+                  (logits.scalar_type() == at::kFloat || logits.scalar_type() == at::kBFloat16 ||
+                   logits.scalar_type() == at::kHalf),
+              "logits must be a CUDA FP32/BF16/FP16 matrix with dense rows");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  const int64_t n = num_draft_tokens.numel();
+  for (const auto& t : {cu_num_logits, query_start_loc, num_draft_tokens, seq_lens, prefill_len}) {
+    TORCH_CHECK(t.device() == logits.device() && t.scalar_type() == at::kInt && t.is_contiguous() && t.dim() == 1,
+                "request metadata must be contiguous CUDA int32 vectors");
+  }
+  TORCH_CHECK(cu_num_logits.numel() == n + 1 && query_start_loc.numel() == n + 1 && seq_lens.numel() == n &&
+                  prefill_len.numel() == n,
+              "invalid request metadata shapes");
+  TORCH_CHECK(input_ids.device() == logits.device() && input_ids.dim() == 1 && input_ids.is_contiguous() &&
+                  (input_ids.scalar_type() == at::kInt || input_ids.scalar_type() == at::kLong),
+              "input_ids must be a contiguous CUDA int32/int64 vector");
+  TORCH_CHECK(sampled.device() == logits.device() && sampled.scalar_type() == input_ids.scalar_type() &&
+                  sampled.dim() == 2 && sampled.size(0) == n && sampled.size(1) >= 1 && sampled.is_contiguous(),
+              "sampled must be a contiguous [requests, steps+1] tensor of the input_ids dtype");
+  for (const auto& t : {num_sampled, num_rejected}) {
+    TORCH_CHECK(t.device() == logits.device() && t.scalar_type() == at::kInt && t.is_contiguous() &&
+                    t.dim() == 1 && t.numel() == n,
+                "num_sampled and num_rejected must be contiguous CUDA int32 [requests]");
+  }
+  if (n == 0) return;
+  const int logits_dtype = logits.scalar_type() == at::kFloat      ? LD_DTYPE_F32
+                           : logits.scalar_type() == at::kBFloat16 ? LD_DTYPE_BF16
+                                                                   : LD_DTYPE_F16;
+  const int token_dtype = input_ids.scalar_type() == at::kLong ? LD_DTYPE_I64 : LD_DTYPE_I32;
+  check_rc(ld_greedy_verify(logits.data_ptr(), logits_dtype, logits.size(0), logits.size(1), logits.stride(0),
+                            cu_num_logits.data_ptr<int32_t>(), query_start_loc.data_ptr<int32_t>(),
+                            input_ids.data_ptr(), token_dtype, input_ids.numel(),
+                            num_draft_tokens.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
+                            prefill_len.data_ptr<int32_t>(), n, sampled.size(1) - 1, sampled.data_ptr(),
+                            num_sampled.data_ptr<int32_t>(), num_rejected.data_ptr<int32_t>(), stream_of(logits)));
+}
+
 }  // namespace lightdelta_b200
 
 TORCH_LIBRARY(lightdelta, m) {
@@ -146,6 +189,10 @@ TORCH_LIBRARY(lightdelta, m) {
   m.def("gather_state(Tensor pool, Tensor slots, Tensor valid, Tensor(o!) out) -> ()");
   m.def("scatter_state(Tensor packed, Tensor slots, Tensor(p!) pool) -> ()");
   m.def("copy_state(Tensor(p!) pool, Tensor src, Tensor dst) -> ()");
+  m.def(
+      "greedy_verify(Tensor logits, Tensor cu_num_logits, Tensor query_start_loc, Tensor input_ids, "
+      "Tensor num_draft_tokens, Tensor seq_lens, Tensor prefill_len, Tensor(a!) sampled, "
+      "Tensor(b!) num_sampled, Tensor(c!) num_rejected) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(lightdelta, CUDA, m) {
@@ -153,4 +200,5 @@ TORCH_LIBRARY_IMPL(lightdelta, CUDA, m) {
   m.impl("gather_state", lightdelta_b200::gather_state);
   m.impl("scatter_state", lightdelta_b200::scatter_state);
   m.impl("copy_state", lightdelta_b200::copy_state);
+  m.impl("greedy_verify", lightdelta_b200::greedy_verify);
 }

@@ -41,3 +41,9 @@ def _scatter_fake(packed, slots, pool):
 @torch.library.register_fake("lightdelta::copy_state")
 def _copy_fake(pool, src, dst):
     return None
+
+
+@torch.library.register_fake("lightdelta::greedy_verify")
+def _greedy_verify_fake(logits, cu_num_logits, query_start_loc, input_ids, num_draft_tokens, seq_lens, prefill_len,
+                        sampled, num_sampled, num_rejected):
+    return None

@@ -6,6 +6,8 @@ No public dataset exists for this path; these builders restate the configuration
   config 3  MTP verify, B=64, T=4, accepted ~ U{1..4}, distinct slots per (request, step)
   config 4  state-pool copy, pools of 2048 slots, gather 512 slots then scatter to a permutation
   config 5  stacked decode over 48 layers (T=4 verify), state sharded by sequence slot
+  sampling  config 3's greedy draft verification: 64 requests x 3 drafts, 4 logits rows each over
+            a 151,936-token (Qwen3) vocabulary, accepted drafts ~ U{0..3}
 Geometry: H=16 key heads, HV=32 value heads (ratio 2), K=V=128.  q, k, v ~ N(0,1) bf16; a_log =
 dt_bias = 0 so g = -softplus(a) with a ~ N(0,1); b ~ N(0,1) (beta = sigmoid(b)); gate 0.2*N(0,1);
 norm weight N(0,1) bf16; state fp32 N(0, 0.02^2).  qkv and gate are slices of one wider
@@ -186,3 +188,74 @@ def config4_indices(device, seed: int = 4, pool_slots: int = 2048, count: int = 
     gather = (torch.randperm(pool_slots - 1, device=device, generator=gen)[:count] + 1).to(torch.int32)
     scatter = (torch.randperm(pool_slots - 1, device=device, generator=gen)[:count] + 1).to(torch.int32)
     return gather, scatter
+
+
+@dataclass
+class SamplingCase:
+    """Arguments of torch.ops.lightdelta.greedy_verify over several logits buffers.
+
+    `logits` holds `buffers` independent [rows, vocab] matrices so that cycling through them
+    reads more than the 126 MB L2 between two uses of the same buffer.
+    """
+
+    logits: list
+    cu_num_logits: torch.Tensor
+    query_start_loc: torch.Tensor
+    input_ids: torch.Tensor
+    num_draft_tokens: torch.Tensor
+    seq_lens: torch.Tensor
+    prefill_len: torch.Tensor
+    sampled: torch.Tensor
+    num_sampled: torch.Tensor
+    num_rejected: torch.Tensor
+
+    def op_args(self, buffer: int) -> tuple:
+        return (self.logits[buffer], self.cu_num_logits, self.query_start_loc, self.input_ids,
+                self.num_draft_tokens, self.seq_lens, self.prefill_len, self.sampled, self.num_sampled,
+                self.num_rejected)
+
+    @property
+    def requests(self) -> int:
+        return self.num_draft_tokens.numel()
+
+    def bytes_per_launch(self) -> int:
+        """Logits rows read (every row is consulted when all requests have steps + 1 rows)."""
+        rows, vocab = self.logits[0].shape
+        return rows * vocab * self.logits[0].element_size()
+
+
+def sampling_case(device, seed: int = 6, requests: int = 64, steps: int = 3, vocab: int = 151936,
+                  dtype: torch.dtype = torch.float32, buffers: int = 4) -> SamplingCase:
+    """Config-3 verification: every request has `steps` drafts and steps + 1 logits rows; a seeded
+    prefix of U{0..steps} drafts is planted as the row maximum, the rest of each row is N(0,1)."""
+    gen = torch.Generator(device="cpu")
+    gen.manual_seed(seed)
+    drafts = torch.full((requests,), steps, dtype=torch.int32)
+    rows = steps + 1
+    cu = torch.arange(0, requests * rows + 1, rows, dtype=torch.int32)
+    qsl = cu.clone()  # one accepted token + the drafts per request
+    input_ids = torch.randint(0, vocab, (requests * rows,), generator=gen, dtype=torch.int32)
+    logits = []
+    for b in range(buffers):
+        accepted = torch.randint(0, steps + 1, (requests,), generator=gen)
+        planted = torch.randint(0, vocab, (requests, rows), generator=gen)
+        drafts_of = input_ids.view(requests, rows)[:, 1:]
+        for i in range(steps):
+            take = accepted > i
+            planted[take, i] = drafts_of[take, i].long()
+        matrix = torch.empty(requests * rows, vocab, device=device, dtype=torch.float32)
+        matrix.normal_(generator=torch.Generator(device=device).manual_seed(seed * 100 + b))
+        matrix.view(requests, rows, vocab).scatter_(2, planted.to(device)[:, :, None], 8.0)
+        logits.append(matrix.to(dtype))
+    return SamplingCase(
+        logits=logits,
+        cu_num_logits=cu.to(device),
+        query_start_loc=qsl.to(device),
+        input_ids=input_ids.to(device),
+        num_draft_tokens=drafts.to(device),
+        seq_lens=torch.full((requests,), 4096, dtype=torch.int32, device=device),
+        prefill_len=torch.zeros(requests, dtype=torch.int32, device=device),
+        sampled=torch.empty(requests, steps + 1, dtype=torch.int32, device=device),
+        num_sampled=torch.empty(requests, dtype=torch.int32, device=device),
+        num_rejected=torch.empty(requests, dtype=torch.int32, device=device),
+    )

@@ -12,6 +12,7 @@ Functions and the reference code they restate:
   gather_state       csrc/state_io.cu:11-27, :44-58
   scatter_state      csrc/state_io.cu:11-27, :60-69
   copy_slots         python/lightdelta/backend.py:87-91 for states already in the pool
+  greedy_verify      python/lightdelta/runtime/speculation.py:274-326 (oracle/greedy_oracle.c)
 """
 
 from __future__ import annotations
@@ -35,7 +36,7 @@ def build(force: bool = False) -> Path:
     stale = (
         force
         or not LIB_PATH.exists()
-        or any(p.stat().st_mtime > LIB_PATH.stat().st_mtime for p in (HERE / "gdn_oracle.c", HERE / "Makefile"))
+        or any(p.stat().st_mtime > LIB_PATH.stat().st_mtime for p in (HERE / "gdn_oracle.c", HERE / "greedy_oracle.c", HERE / "Makefile"))
     )
     if stale:
         subprocess.run(["make", "-s", "-C", str(HERE)] + (["-B"] if force else []), check=True)
@@ -61,6 +62,10 @@ def lib() -> ctypes.CDLL:
         handle.oracle_scatter_state.restype = None
         handle.oracle_copy_slots.argtypes = [p, i64, i64, p, i64, p, i64, i64, i64]
         handle.oracle_copy_slots.restype = None
+        handle.oracle_argmax_rows.argtypes = [p, i32, i64, i64, i64, p, i32]
+        handle.oracle_argmax_rows.restype = None
+        handle.oracle_greedy_verify.argtypes = [p, i32, i64, i64, i64, p, p, p, i64, p, p, p, i64, i64, p, p, p, p, i32]
+        handle.oracle_greedy_verify.restype = ctypes.c_uint32
         _lib = handle
     return _lib
 
@@ -194,3 +199,53 @@ def copy_slots(pool: np.ndarray, src: np.ndarray, dst: np.ndarray) -> None:
     dst, dst_stride = _vector(dst)
     lib().oracle_copy_slots(_ptr(pool), pool.shape[0], pool_stride, _ptr(src), src_stride, _ptr(dst), dst_stride,
                             src.shape[0], elems)
+
+
+# ---------------------------------------------------------------------------------------------
+# greedy MTP verification (speculation.py:274-326)
+# ---------------------------------------------------------------------------------------------
+VERIFY_FAULT_DRAFTS = 0x40
+VERIFY_FAULT_RANGE = 0x80
+
+
+def _logits_view(logits: np.ndarray) -> tuple[np.ndarray, int, int]:
+    """(array, dtype code, row stride in elements); bf16 / f16 travel as uint16 bits."""
+    if logits.ndim != 2 or logits.strides[1] != logits.itemsize:
+        raise TypeError("logits must be a matrix with a dense last dimension")
+    if logits.dtype == np.float32:
+        code = 0
+    elif logits.dtype == np.uint16:
+        code = 1  # bf16 bits
+    elif logits.dtype == np.float16:
+        code = 2
+    else:
+        raise TypeError(f"unsupported logits dtype {logits.dtype}")
+    return logits, code, logits.strides[0] // logits.itemsize
+
+
+def argmax_rows(logits: np.ndarray, threads: int = 0) -> np.ndarray:
+    """torch.argmax(logits, -1) for float32, float16 or bf16-bits (uint16) rows."""
+    logits, code, stride = _logits_view(logits)
+    target = np.empty(logits.shape[0], np.int64)
+    lib().oracle_argmax_rows(_ptr(logits), code, logits.shape[0], logits.shape[1], stride, _ptr(target), threads)
+    return target
+
+
+def greedy_verify(logits, cu_num_logits, query_start_loc, input_ids, num_draft_tokens, seq_lens, prefill_len,
+                  num_speculative_steps: int, threads: int = 0):
+    """Returns (sampled int64 [R, steps+1], num_sampled int32 [R], num_rejected int32 [R], faults)."""
+    logits, code, stride = _logits_view(logits)
+    cu_num_logits, query_start_loc, num_draft_tokens, seq_lens, prefill_len = (
+        _dense(x, np.int32) for x in (cu_num_logits, query_start_loc, num_draft_tokens, seq_lens, prefill_len))
+    input_ids = _dense(input_ids, np.int64)
+    n = num_draft_tokens.shape[0]
+    sampled = np.empty((n, num_speculative_steps + 1), np.int64)
+    num_sampled = np.empty(n, np.int32)
+    num_rejected = np.empty(n, np.int32)
+    target = np.empty(max(1, logits.shape[0]), np.int64)
+    faults = lib().oracle_greedy_verify(
+        _ptr(logits), code, logits.shape[0], logits.shape[1], stride, _ptr(cu_num_logits), _ptr(query_start_loc),
+        _ptr(input_ids), input_ids.shape[0], _ptr(num_draft_tokens), _ptr(seq_lens), _ptr(prefill_len), n,
+        num_speculative_steps, _ptr(sampled), _ptr(num_sampled), _ptr(num_rejected), _ptr(target), threads,
+    )
+    return sampled, num_sampled, num_rejected, int(faults)

@@ -41,8 +41,26 @@ BACKEND_CASES = [
 ]
 
 
+SAMPLER_CASES = [
+    # Greedy MTP verification (speculation.py:274-326): mixed draft counts, short logits spans,
+    # a request without logits, prefill rows, ties, NaN / +-inf rows; int64 tokens as in the
+    # reference's own test (tests/test_runtime.py:7-23).
+    dict(name="sampler_f32_mixed", seed=101, requests=48, steps=3, vocab=2053, dtype="f32", tokens="i64",
+         ties_per_row=1),
+    # bf16 logits with several equal maxima per row and int32 tokens (vLLM's input_ids dtype).
+    dict(name="sampler_bf16_ties", seed=103, requests=32, steps=3, vocab=4096, dtype="bf16", tokens="i32",
+         ties_per_row=3),
+    # fp16 logits, seven draft tokens (LD_MAX_VERIFY_STEPS), odd vocabulary.
+    dict(name="sampler_f16_steps7", seed=107, requests=20, steps=7, vocab=1537, dtype="f16", tokens="i32",
+         ties_per_row=1),
+    # Qwen3 vocabulary size: the argmax spans several CTAs of a cluster.
+    dict(name="sampler_f32_vocab151936", seed=109, requests=12, steps=3, vocab=151936, dtype="f32", tokens="i32",
+         ties_per_row=1),
+]
+
+
 def spec_by_name(name: str) -> dict:
-    for spec in POST_CONV_CASES + BACKEND_CASES:
+    for spec in POST_CONV_CASES + BACKEND_CASES + SAMPLER_CASES:
         if spec["name"] == name:
             return spec
     raise KeyError(name)
@@ -128,3 +146,75 @@ def backend_case(spec: dict) -> dict:
     else:
         raise ValueError(spec["mutation"])
     return dict(arrays=arrays, rows=rows, hv=hv, h=h, qkv_width=qkv_width)
+
+
+def sampler_case(spec: dict) -> dict:
+    """Inputs of a LightDeltaRejectionSampler call (speculation.py:274-326) as numpy arrays.
+
+    logits are float32 values already rounded to the case's dtype ("f32", "bf16", "f16");
+    cu_num_logits / query_start_loc / num_draft_tokens / seq_lens / prefill_len are int32,
+    input_ids int64 (cast to the case's token dtype by the caller).  Each request's logits
+    rows plant the draft tokens as the row maximum for a seeded accepted prefix, then a
+    mismatch; some rows add equal maxima (ties), NaN or +-inf.
+    """
+    R, steps, vocab = spec["requests"], spec["steps"], spec["vocab"]
+    s = spec["seed"] * 100
+    u = lambda k, n: detrand.uniform(s + k, n)  # noqa: E731
+    drafts = detrand.integers(s + 1, R, steps + 1)
+    short = u(2, R) < 0.15
+    rows = np.where(short & (drafts > 0), drafts, drafts + 1)
+    if R > 5:  # a request with drafts but no logits rows: the bonus comes from target[end - 1]
+        drafts[5], rows[5] = 2, 0
+    accepted = (u(3, R) * (drafts + 1)).astype(np.int64)
+    extra_inputs = np.where(u(4, R) < 0.25, 2, 0)
+    inputs = drafts + 1 + extra_inputs
+    seq_lens = 1 + detrand.integers(s + 5, R, 1000)
+    prefill = u(6, R) < 0.2
+    prefill_len = np.where(prefill, seq_lens + 1, 0)
+
+    query_start_loc = np.concatenate([[0], np.cumsum(inputs)]).astype(np.int32)
+    input_ids = detrand.integers(s + 7, int(inputs.sum()), vocab)
+    cu = np.concatenate([[0], np.cumsum(rows)]).astype(np.int32)
+    n_logits = int(cu[-1]) + 3  # three trailing rows that no request consults
+    logits = detrand.normal(s + 8, (n_logits, vocab))
+
+    total_rows = n_logits
+    planted_random = detrand.integers(s + 9, total_rows, vocab)
+    shift = 1 + detrand.integers(s + 10, total_rows, vocab - 1)
+    tie_pos = detrand.integers(s + 11, total_rows * max(1, spec["ties_per_row"]), vocab).reshape(total_rows, -1)
+    row_kind = u(12, total_rows)
+    special_pos = detrand.integers(s + 13, total_rows, vocab)
+    for r in range(R):
+        draft = input_ids[query_start_loc[r + 1] - drafts[r]: query_start_loc[r + 1]]
+        for i in range(rows[r]):
+            row = cu[r] + i
+            if i < accepted[r] and i < drafts[r]:
+                token = draft[i]
+            elif i < drafts[r]:
+                token = (draft[i] + shift[row]) % vocab
+            else:
+                token = planted_random[row]
+            logits[row, token] = 6.0
+    for row in range(total_rows):
+        kind = row_kind[row]
+        if kind < 0.25:  # equal maxima: the first index wins
+            logits[row, tie_pos[row]] = logits[row].max()
+        elif kind < 0.31:
+            logits[row, special_pos[row]] = np.nan
+        elif kind < 0.34:
+            logits[row, :] = -np.inf
+        elif kind < 0.37:
+            logits[row, special_pos[row]] = np.inf
+    if spec["dtype"] == "bf16":
+        logits = detrand.bf16_values(detrand.bf16_bits(logits))
+    elif spec["dtype"] == "f16":
+        logits = logits.astype(np.float16).astype(np.float32)
+    return dict(
+        logits=logits.astype(np.float32),
+        cu_num_logits=cu,
+        query_start_loc=query_start_loc,
+        input_ids=input_ids.astype(np.int64),
+        num_draft_tokens=drafts.astype(np.int32),
+        seq_lens=seq_lens.astype(np.int32),
+        prefill_len=prefill_len.astype(np.int32),
+    )

@@ -11,6 +11,9 @@ It imports the reference's own Python code (torch only, on the CPU):
     (tests/test_gdn.py:58-122; python/lightdelta/backend.py:30-91).  The reference module
     ``lightdelta.ops`` only loads the compiled ``_C`` library, which that path never calls, so
     it is replaced by an empty module while the fixtures are made.
+  * LightDeltaRejectionSampler (python/lightdelta/runtime/speculation.py:271-326), loaded from
+    its file with the vLLM modules it imports at the top replaced by empty stand-ins: the
+    sampler itself uses torch only.
 Inputs are regenerated from seeds by tests/golden/detrand.py, so a fixture stores only its
 case parameters and the reference's results: full bf16 outputs and, for states, values at
 seeded sample positions (a few hundred per slot).  Nothing here runs on the GPU box.
@@ -112,14 +115,90 @@ def make_backend(GDNBackend, BackendConfig) -> None:
         print(spec["name"], {k: v.shape for k, v in record.items()})
 
 
+class _Stub(types.ModuleType):
+    """Module whose every attribute is a placeholder class (import-time names only)."""
+
+    def __getattr__(self, name):
+        if name.startswith("__"):
+            raise AttributeError(name)
+        return type(name, (), {})
+
+
+class _SamplerOutput:
+    FIELDS = ("sampled_token_ids", "logprobs_tensors", "num_nans", "num_sampled", "num_rejected")
+
+    def __init__(self, *values):
+        for field, value in zip(self.FIELDS, values):
+            setattr(self, field, value)
+
+
+def _import_sampler(path: str):
+    import importlib.util
+
+    names = ["vllm", "vllm.config", "vllm.config.compilation", "vllm.forward_context", "vllm.model_executor",
+             "vllm.model_executor.layers", "vllm.model_executor.layers.attention_layer_base", "vllm.v1",
+             "vllm.v1.worker", "vllm.v1.worker.gpu", "vllm.v1.worker.gpu.attn_utils",
+             "vllm.v1.worker.gpu.input_batch", "vllm.v1.worker.gpu.sample", "vllm.v1.worker.gpu.sample.output",
+             "vllm.v1.worker.gpu.spec_decode", "vllm.v1.worker.gpu.spec_decode.eagle",
+             "vllm.v1.worker.gpu.spec_decode.eagle.utils"]
+    saved = {name: sys.modules.get(name) for name in names}
+    for name in names:
+        sys.modules[name] = _Stub(name)
+    sys.modules["vllm.v1.worker.gpu.sample.output"].SamplerOutput = _SamplerOutput
+    try:
+        file = Path(path) / "lightdelta" / "runtime" / "speculation.py"
+        spec = importlib.util.spec_from_file_location("reference_speculation", file)
+        module = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(module)
+    finally:
+        for name, module_before in saved.items():
+            if module_before is None:
+                sys.modules.pop(name, None)
+            else:
+                sys.modules[name] = module_before
+    return module.LightDeltaRejectionSampler
+
+
+def make_sampler(LightDeltaRejectionSampler) -> None:
+    from types import SimpleNamespace
+
+    dtypes = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}
+    for spec in cases.SAMPLER_CASES:
+        case = cases.sampler_case(spec)
+        token_dtype = torch.int64 if spec["tokens"] == "i64" else torch.int32
+        batch = SimpleNamespace(
+            num_reqs=spec["requests"],
+            num_draft_tokens_per_req=case["num_draft_tokens"].copy(),
+            input_ids=torch.from_numpy(case["input_ids"]).to(token_dtype),
+            query_start_loc=torch.from_numpy(case["query_start_loc"]),
+            cu_num_logits=torch.from_numpy(case["cu_num_logits"]),
+            seq_lens=torch.from_numpy(case["seq_lens"]),
+            prefill_len_np=case["prefill_len"].copy(),
+        )
+        logits = torch.from_numpy(case["logits"]).to(dtypes[spec["dtype"]])
+        output = LightDeltaRejectionSampler(spec["steps"])(logits, batch)
+        record = {
+            "target": logits.argmax(dim=-1).numpy(),  # speculation.py:279
+            "sampled": output.sampled_token_ids.to(torch.int64).numpy(),
+            "num_sampled": output.num_sampled.numpy(),
+            "num_rejected": output.num_rejected.numpy(),
+        }
+        np.savez_compressed(HERE / f"{spec['name']}.npz", **record)
+        print(spec["name"], {k: v.shape for k, v in record.items()})
+
+
 def main() -> int:
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", required=True, help="path of the reference's python/ directory")
+    parser.add_argument("--only", choices=("all", "gdn", "sampler"), default="all")
     args = parser.parse_args()
     torch.set_num_threads(8)
-    GDNBackend, BackendConfig, GDNInputs, post_conv_gdn = _import_reference(args.reference)
-    make_post_conv(post_conv_gdn, GDNInputs)
-    make_backend(GDNBackend, BackendConfig)
+    if args.only in ("all", "gdn"):
+        GDNBackend, BackendConfig, GDNInputs, post_conv_gdn = _import_reference(args.reference)
+        make_post_conv(post_conv_gdn, GDNInputs)
+        make_backend(GDNBackend, BackendConfig)
+    if args.only in ("all", "sampler"):
+        make_sampler(_import_sampler(args.reference))
     return 0
 
 

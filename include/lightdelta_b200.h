@@ -167,6 +167,16 @@ int ld_copy_slots(float* pool, int64_t n_pool_slots, int64_t pool_slot_stride,
 int ld_decode_kernel_override(int variant);
 
 /*
+ * Programmatic dependent launch (PDL), process-wide: 1 (the default) launches every kernel
+ * with programmatic stream serialisation, so its CTAs may be scheduled while the preceding
+ * kernel on the stream finishes; each kernel waits (griddepcontrol.wait) for that kernel's
+ * completion and memory before touching global memory, so results and ordering are unchanged.
+ * 0 launches with plain stream order; -1 only queries.  Returns the previous setting.
+ * No counterpart in the reference.
+ */
+int ld_programmatic_launch(int enable);
+
+/*
  * Reads (and, if clear != 0, resets) the device fault word of the current device into *flags.
  * This call synchronises the device; it is a diagnostic, not part of the hot path.
  */

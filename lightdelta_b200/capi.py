@@ -76,6 +76,8 @@ def lib() -> ctypes.CDLL:
     handle.ld_greedy_verify.restype = i32
     handle.ld_greedy_verify_cluster_override.argtypes = [i32]
     handle.ld_greedy_verify_cluster_override.restype = i32
+    handle.ld_programmatic_launch.argtypes = [i32]
+    handle.ld_programmatic_launch.restype = i32
     _lib = handle
     return handle
 
@@ -107,6 +109,12 @@ def set_decode_kernel(name: str) -> str:
     if previous < 0:
         raise LightDeltaError(-previous, last_error())
     return {v: k for k, v in DECODE_KERNELS.items()}[previous]
+
+
+def set_programmatic_launch(enable: bool) -> bool:
+    """Enable or disable programmatic dependent launch for every kernel; returns the previous
+    setting.  Results do not depend on it."""
+    return bool(lib().ld_programmatic_launch(1 if enable else 0))
 
 
 def set_verify_cluster(cluster: int) -> int:

@@ -1,4 +1,5 @@
 // Library-wide C entry points: error reporting, version and the device fault word.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <string>
@@ -9,7 +10,10 @@
 namespace ldb {
 namespace {
 thread_local std::string g_last_error;
+std::atomic<int> g_programmatic_launch{1};
 }  // namespace
+
+bool programmatic_launch_enabled() { return g_programmatic_launch.load(std::memory_order_relaxed) != 0; }
 
 int set_error(int code, const char* fmt, ...) {
   char buffer[512];
@@ -33,6 +37,11 @@ const char* last_error() { return g_last_error.c_str(); }
 extern "C" const char* ld_last_error(void) { return ldb::last_error(); }
 
 extern "C" const char* ld_version(void) { return "lightdelta_b200 0.1.0 (sm_100a)"; }
+
+extern "C" int ld_programmatic_launch(int enable) {
+  if (enable < 0) return ldb::g_programmatic_launch.load();
+  return ldb::g_programmatic_launch.exchange(enable != 0 ? 1 : 0);
+}
 
 extern "C" int ld_fault_flags(uint32_t* flags, int clear) {
   if (flags == nullptr) return ldb::set_error(LD_ERR_INVALID, "ld_fault_flags: flags is NULL");

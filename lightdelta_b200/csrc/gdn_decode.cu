@@ -38,6 +38,7 @@
 #include <mutex>
 
 #include "internal.h"
+#include "launch.cuh"
 #include "lightdelta_b200.h"
 
 namespace ldb {
@@ -277,6 +278,8 @@ __device__ __forceinline__ void gated_rmsnorm_store(const float* o_row, const fl
 // ==========================================================================================
 template <bool kVecAct>
 __global__ void __launch_bounds__(Tile<4>::kThreads, 2) gdn_decode_rowreg_kernel(const DecodeArgs p) {
+  ldb::grid_dependency_wait();
+  ldb::allow_dependent_launch();
   __shared__ float4 sh_q[kMaxTokens][kDim / 4];
   __shared__ float4 sh_k[kMaxTokens][kDim / 4];
   __shared__ float sh_v[kMaxTokens][kDim];
@@ -795,6 +798,8 @@ __device__ void consume(const DecodeArgs& p, Smem& sm, int tid) {
 // sub-partitions (at most 3 warps each), which allows 168 registers per thread.
 template <int kRows>
 __global__ void __maxnreg__(168) gdn_decode_stream_kernel(const DecodeArgs p) {
+  ldb::grid_dependency_wait();
+  ldb::allow_dependent_launch();
   constexpr int kConsumers = Tile<kRows>::kThreads;
   constexpr int kConsumerWarps = kConsumers / 32;
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -1043,6 +1048,8 @@ __device__ void store_loop(Smem<kLoads, kStaging>& sm, int lane) {
 // Block: 256 consumer threads, one producer warp, one storer warp; one CTA per SM.
 template <int kLoads, int kStaging>
 __global__ void __maxnreg__(168) gdn_decode_tmastore_kernel(const DecodeArgs p) {
+  ldb::grid_dependency_wait();
+  ldb::allow_dependent_launch();
   extern __shared__ __align__(128) unsigned char smem_raw[];
   using S = Smem<kLoads, kStaging>;
   S& sm = *reinterpret_cast<S*>(smem_raw);
@@ -1323,6 +1330,8 @@ __device__ __forceinline__ void staged_body(const DecodeArgs& p, Smem<Q>& sm) {
 
 template <int Q>
 __global__ void __cluster_dims__(Q, 1, 1) __launch_bounds__(kThreads, 3) gdn_decode_staged_kernel(const DecodeArgs p) {
+  ldb::grid_dependency_wait();
+  ldb::allow_dependent_launch();
   extern __shared__ __align__(128) unsigned char smem_raw[];
   staged_body<Q>(p, *reinterpret_cast<Smem<Q>*>(smem_raw));
 }
@@ -1505,39 +1514,41 @@ extern "C" int ld_decode(const void* qkv, int64_t qkv_row_stride, const void* a,
     // SM, and has the lowest latency for small launches.
     variant = (width == 1 && args.total_items >= 2 * info.sms) ? LD_DECODE_KERNEL_STREAM : LD_DECODE_KERNEL_ROWREG;
   }
+  cudaError_t err;
   if (variant != LD_DECODE_KERNEL_ROWREG) {
-    const unsigned int grid = static_cast<unsigned int>(std::min<int64_t>(args.total_items, info.sms));
+    const dim3 grid(static_cast<unsigned int>(std::min<int64_t>(args.total_items, info.sms)));
+    const dim3 items(static_cast<unsigned int>(args.total_items));
     if (variant == LD_DECODE_KERNEL_STAGED_Q1) {
-      stream::staged::gdn_decode_staged_kernel<1>
-          <<<static_cast<unsigned int>(args.total_items), stream::staged::kThreads, sizeof(stream::staged::Smem<1>), s>>>(args);
+      err = ldb::launch(stream::staged::gdn_decode_staged_kernel<1>, items, dim3(stream::staged::kThreads),
+                        sizeof(stream::staged::Smem<1>), s, 1, args);
     } else if (variant == LD_DECODE_KERNEL_STAGED_Q2) {
-      stream::staged::gdn_decode_staged_kernel<2><<<static_cast<unsigned int>(2 * args.total_items),
-                                                    stream::staged::kThreads, sizeof(stream::staged::Smem<2>), s>>>(args);
+      err = ldb::launch(stream::staged::gdn_decode_staged_kernel<2>, dim3(2 * items.x), dim3(stream::staged::kThreads),
+                        sizeof(stream::staged::Smem<2>), s, 1, args);
     } else if (variant == LD_DECODE_KERNEL_STAGED_Q4) {
-      stream::staged::gdn_decode_staged_kernel<4><<<static_cast<unsigned int>(4 * args.total_items),
-                                                    stream::staged::kThreads, sizeof(stream::staged::Smem<4>), s>>>(args);
+      err = ldb::launch(stream::staged::gdn_decode_staged_kernel<4>, dim3(4 * items.x), dim3(stream::staged::kThreads),
+                        sizeof(stream::staged::Smem<4>), s, 1, args);
     } else if (variant == LD_DECODE_KERNEL_TMA_STORE) {
       if (width == 1) {
-        stream::ts::gdn_decode_tmastore_kernel<2, 1><<<grid, stream::ts::kThreads, sizeof(stream::ts::Smem<2, 1>), s>>>(
-            args);
+        err = ldb::launch(stream::ts::gdn_decode_tmastore_kernel<2, 1>, grid, dim3(stream::ts::kThreads),
+                          sizeof(stream::ts::Smem<2, 1>), s, 1, args);
       } else {
-        stream::ts::gdn_decode_tmastore_kernel<1, 2><<<grid, stream::ts::kThreads, sizeof(stream::ts::Smem<1, 2>), s>>>(
-            args);
+        err = ldb::launch(stream::ts::gdn_decode_tmastore_kernel<1, 2>, grid, dim3(stream::ts::kThreads),
+                          sizeof(stream::ts::Smem<1, 2>), s, 1, args);
       }
     } else {
-      stream::gdn_decode_stream_kernel<4><<<grid, Tile<4>::kThreads + 32, sizeof(stream::Smem), s>>>(args);
+      err = ldb::launch(stream::gdn_decode_stream_kernel<4>, grid, dim3(Tile<4>::kThreads + 32), sizeof(stream::Smem),
+                        s, 1, args);
     }
   } else {
     const bool vec_act = aligned(qkv, 8) && qkv_row_stride % 4 == 0 && aligned(gate, 8) &&
                          gate_row_stride % 4 == 0 && aligned(out, 8);
     const dim3 grid(static_cast<unsigned int>(args.total_items));
     if (vec_act) {
-      gdn_decode_rowreg_kernel<true><<<grid, Tile<4>::kThreads, 0, s>>>(args);
+      err = ldb::launch(gdn_decode_rowreg_kernel<true>, grid, dim3(Tile<4>::kThreads), 0, s, 1, args);
     } else {
-      gdn_decode_rowreg_kernel<false><<<grid, Tile<4>::kThreads, 0, s>>>(args);
+      err = ldb::launch(gdn_decode_rowreg_kernel<false>, grid, dim3(Tile<4>::kThreads), 0, s, 1, args);
     }
   }
-  const cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) {
     return set_error(LD_ERR_CUDA, "decode launch failed: %s", cudaGetErrorString(err));
   }

@@ -30,6 +30,7 @@
 #include <cstring>
 
 #include "internal.h"
+#include "launch.cuh"
 #include "lightdelta_b200.h"
 
 namespace {
@@ -377,6 +378,8 @@ __device__ __forceinline__ void scan_row_pair(const T* row0, const T* row1, bool
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads) greedy_verify_kernel(const VerifyArgs p) {
+  ldb::grid_dependency_wait();
+  ldb::allow_dependent_launch();
   __shared__ float warp_value[kMaxRows][kWarps];
   __shared__ int warp_index[kMaxRows][kWarps];
   __shared__ float slice_value[kMaxCluster][kMaxRows];  // rank 0: one entry per cluster rank
@@ -459,41 +462,37 @@ int device_sms() {
   return sms;
 }
 
-// Cluster size: enough CTAs for about eight per SM across the launch, at most 8 (the portable
-// cluster limit), and slices of at least 4096 elements.
-int pick_cluster(int64_t n_requests, int64_t vocab, int sms) {
+// Cluster size: the largest Q (at most 8, the portable cluster limit) whose R x Q CTAs all fit
+// on the GPU at once, so the launch runs as one wave, with slices of at least 4096 elements.
+int pick_cluster(int64_t n_requests, int64_t vocab, int64_t resident_ctas) {
   const int forced = g_cluster_override.load(std::memory_order_relaxed);
   if (forced > 0) return forced;
-  int q = 1;
-  while (q < 8 && n_requests * q < 8LL * sms && vocab / (2 * q) >= 4096) q *= 2;
+  int q = 8;
+  while (q > 1 && (n_requests * q > resident_ctas || vocab / (2 * q) < 4096)) q /= 2;
   return q;
 }
 
 template <typename T>
-cudaError_t launch(const VerifyArgs& args, int q, cudaStream_t stream) {
-  const dim3 grid(static_cast<unsigned int>(args.n_requests * q));
-  if (q == 1) {
-    greedy_verify_kernel<T><<<grid, kThreads, 0, stream>>>(args);
-    return cudaGetLastError();
-  }
+int resident_ctas_per_sm() {
+  static const int blocks = [] {
+    int b = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, greedy_verify_kernel<T>, kThreads, 0) != cudaSuccess) b = 1;
+    return b > 0 ? b : 1;
+  }();
+  return blocks;
+}
+
+template <typename T>
+cudaError_t launch_verify(VerifyArgs args, int sms, cudaStream_t stream) {
+  const int q = pick_cluster(args.n_requests, args.vocab, static_cast<int64_t>(resident_ctas_per_sm<T>()) * sms);
+  args.chunk = ((args.vocab + q - 1) / q + 7) / 8 * 8;
   if (q > 8) {  // 16-CTA clusters are a non-portable size that each kernel opts into
     const cudaError_t err =
         cudaFuncSetAttribute(greedy_verify_kernel<T>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (err != cudaSuccess) return err;
   }
-  cudaLaunchConfig_t config = {};
-  config.gridDim = grid;
-  config.blockDim = dim3(kThreads);
-  config.dynamicSmemBytes = 0;
-  config.stream = stream;
-  cudaLaunchAttribute attribute[1];
-  attribute[0].id = cudaLaunchAttributeClusterDimension;
-  attribute[0].val.clusterDim.x = static_cast<unsigned int>(q);
-  attribute[0].val.clusterDim.y = 1;
-  attribute[0].val.clusterDim.z = 1;
-  config.attrs = attribute;
-  config.numAttrs = 1;
-  return cudaLaunchKernelEx(&config, greedy_verify_kernel<T>, args);
+  return ldb::launch(greedy_verify_kernel<T>, dim3(static_cast<unsigned int>(args.n_requests * q)), dim3(kThreads),
+                     0, stream, static_cast<unsigned int>(q), args);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -576,17 +575,15 @@ extern "C" int ld_greedy_verify(const void* logits, int logits_dtype, int64_t n_
   args.num_rejected = num_rejected;
   const int64_t elem = logits_dtype == LD_DTYPE_F32 ? 4 : 2;
   args.vector_ok = aligned16(logits) && (logits_row_stride * elem) % 16 == 0;
-  const int q = pick_cluster(n_requests, vocab, sms);
-  args.chunk = ((vocab + q - 1) / q + 7) / 8 * 8;
 
   auto s = static_cast<cudaStream_t>(stream);
   cudaError_t err;
   if (logits_dtype == LD_DTYPE_F32) {
-    err = launch<float>(args, q, s);
+    err = launch_verify<float>(args, sms, s);
   } else if (logits_dtype == LD_DTYPE_BF16) {
-    err = launch<__nv_bfloat16>(args, q, s);
+    err = launch_verify<__nv_bfloat16>(args, sms, s);
   } else {
-    err = launch<__half>(args, q, s);
+    err = launch_verify<__half>(args, sms, s);
   }
   if (err != cudaSuccess) return set_error(LD_ERR_CUDA, "ld_greedy_verify: launch failed: %s", cudaGetErrorString(err));
   return ldb::ok();

@@ -10,6 +10,9 @@ int set_error(int code, const char* fmt, ...);
 // Clears the calling thread's message and returns LD_OK.
 int ok();
 
+// Whether kernels launch with programmatic dependent launch (ld_programmatic_launch).
+bool programmatic_launch_enabled();
+
 // Per-translation-unit device fault words (see LD_FAULT_* in lightdelta_b200.h).
 int decode_faults(uint32_t* flags, int clear);
 int state_io_faults(uint32_t* flags, int clear);

@@ -15,6 +15,7 @@
 #include <cstdint>
 
 #include "internal.h"
+#include "launch.cuh"
 #include "lightdelta_b200.h"
 
 namespace ldb {
@@ -45,6 +46,8 @@ struct CopyArgs {
 
 template <int kKind, bool kVec>
 __global__ void __launch_bounds__(kCopyThreads) slot_copy_kernel(const CopyArgs p) {
+  ldb::grid_dependency_wait();
+  ldb::allow_dependent_launch();
   const int64_t row = blockIdx.x / p.chunks_per_row;
   const int64_t chunk = blockIdx.x - row * p.chunks_per_row;
   const bool report = chunk == 0 && threadIdx.x == 0;
@@ -128,12 +131,8 @@ int launch_copy(CopyArgs& args, int64_t n, bool vec, void* stream, const char* n
   }
   const dim3 grid(static_cast<unsigned int>(n * args.chunks_per_row));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (vec) {
-    slot_copy_kernel<kKind, true><<<grid, kCopyThreads, 0, s>>>(args);
-  } else {
-    slot_copy_kernel<kKind, false><<<grid, kCopyThreads, 0, s>>>(args);
-  }
-  const cudaError_t err = cudaGetLastError();
+  const cudaError_t err = vec ? ldb::launch(slot_copy_kernel<kKind, true>, grid, dim3(kCopyThreads), 0, s, 1, args)
+                              : ldb::launch(slot_copy_kernel<kKind, false>, grid, dim3(kCopyThreads), 0, s, 1, args);
   if (err != cudaSuccess) return set_error(LD_ERR_CUDA, "%s launch failed: %s", name, cudaGetErrorString(err));
   return ok();
 }

@@ -238,3 +238,33 @@ def test_repeated_in_place_decode(device, kernel):
     torch.cuda.synchronize()
     assert_out_close(bits(case.out), host["out"], "step 3 out")
     assert_state_close(case.pool.cpu().numpy(), host["pool"], "step 3 pool")
+
+
+@pytest.mark.parametrize("variant", ["stream", "rowreg"])
+def test_programmatic_launch_does_not_change_results(device, variant):
+    """Chained in-place decode steps (each reads the states the previous launch wrote), a
+    gather / scatter round trip and a copy, with programmatic dependent launch on and off:
+    bit-identical pools and outputs."""
+    results = []
+    previous_kernel = capi.set_decode_kernel(variant)
+    try:
+        for enable in (True, False):
+            previous = capi.set_programmatic_launch(enable)
+            try:
+                case = workloads.make_decode_case(64, 1, 200, device=device, seed=31)
+                slots = case.slots.flatten()
+                packed = torch.empty(slots.numel(), *case.pool.shape[1:], device=device)
+                for _ in range(5):
+                    torch.ops.lightdelta.decode(*case.op_args())
+                    torch.ops.lightdelta.gather_state(case.pool, slots, torch.ones_like(slots, dtype=torch.bool),
+                                                      packed)
+                    torch.ops.lightdelta.scatter_state(packed, slots.flip(0), case.pool)
+                    torch.ops.lightdelta.copy_state(case.pool, slots[:8], slots[8:16])
+                torch.cuda.synchronize()
+                results.append((case.pool.cpu(), case.out.cpu()))
+            finally:
+                capi.set_programmatic_launch(previous)
+    finally:
+        capi.set_decode_kernel(previous_kernel)
+    assert torch.equal(results[0][0], results[1][0])
+    assert torch.equal(results[0][1].view(torch.int16), results[1][1].view(torch.int16))

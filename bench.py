@@ -9,6 +9,10 @@ Workloads (the default is the one the headline metric is quote
   commit  config 3's explicit commit: copy_state of each sequence's accepted slot to its home slot
   sample  config 3's greedy draft verification (greedy_verify): 64 requests x 3 drafts, 4 fp32
           logits rows each over a 151,936-token vocabulary
+  conv    config 2 with the causal conv1d state update before the decode (conv_decode: the conv
+          kernel, then the decode, in one call): bf16 conv state of width 4 per sequence; the
+          pipeline it replaces (vLLM's conv kernel, then decode) is timed beside it when vLLM is
+          importable
   copy    config 4: gather 512 slots of a 2048-slot layer pool, scatter them to a permuted set
   stacked config 5: 48 layers of T=4 verify over 2048 sequences sharded across the ranks (strong
           scaling), replayed as one CUDA graph per step; run it with a few --steps (~0.2 s each)
@@ -53,7 +57,7 @@ def parse_args(argv=None):
     p.add_argument("--steps", type=int, default=4000)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--workload", choices=("decode", "verify", "commit", "sample", "copy", "stacked"),
+    p.add_argument("--workload", choices=("decode", "verify", "commit", "sample", "conv", "copy", "stacked"),
                    default="decode")
     p.add_argument("--e2e-steps", type=int, default=200)
     p.add_argument("--decode-kernel", choices=("auto", "stream", "rowreg", "tmastore", "staged1", "staged2", "staged4"), default="auto",
@@ -274,6 +278,31 @@ def run_ours(args, dist: Dist) -> dict | None:
         config = {"workload": "config3_commit_copy", "sequences_per_gpu": first.slots.shape[0],
                   "slots_copied_per_step": moved, "pool_slots": pool.shape[0], "batches_in_turn": 4,
                   "note": "a sequence whose accepted slot is its home slot copies nothing"}
+    elif args.workload == "conv":
+        case = workloads.config2(device, seed=2 + seed)
+        conv = workloads.make_conv_state(case, case.pool.shape[0], seed=7 + seed)
+        fused_args = workloads.conv_decode_args(case, conv)
+        requests, width = case.slots.shape
+        tokens = case.tokens
+        hv, h = case.num_v_heads, case.num_k_heads
+        dim = case.qkv.shape[1]
+        conv_width = conv.weight.shape[1]
+        # Per token, besides the decode's bytes: the conv reads the window ((width - 1) bf16
+        # positions of every channel) and the pre-conv row, writes the shifted state
+        # (width - 2 + 1 positions) and the post-conv row.
+        conv_bytes = tokens * dim * 2 * ((conv_width - 1) + (conv_width - 1) + 2)
+        bytes_per_launch = workloads.decode_algorithmic_bytes(requests, width, tokens, h, hv) + conv_bytes
+        touched = requests * 2 * hv * workloads.SLOT_HEAD_BYTES
+
+        def fn():
+            torch.ops.lightdelta.conv_decode(*fused_args)
+
+        units_per_step, unit = tokens, "tokens/s"
+        config = {"workload": "config2_conv_decode", "sequences_per_gpu": requests, "tokens_per_sequence": width,
+                  "num_k_heads": h, "num_v_heads": hv, "conv_width": conv_width, "conv_state_dtype": "bf16",
+                  "conv_layout": "[slots, dim, L]", "launches_per_step": "conv update + decode",
+                  "vllm_pipeline": unfused_conv_decode_us(case, conv, stream)}
+        case = None
     elif args.workload == "sample":
         sampling = workloads.sampling_case(device, seed=6 + seed)
         turn = [0]
@@ -346,8 +375,11 @@ def run_ours(args, dist: Dist) -> dict | None:
     sampler.mark(*window)
     clocks = sampler.summary()
     max_ms = dist.max(total_ms)
+    # Equal-size launches of the dominant kernel per step (the roofline's unit); the conv workload's
+    # two kernels (conv update, decode) are accounted together as one step.
     launches_per_step = {"copy": 2, "stacked": 48}.get(args.workload, 1)
-    kernel_ms = launch_ms / launches_per_step  # equal-size launches within a step
+    kernels_per_step = {"conv": 2}.get(args.workload, launches_per_step)
+    kernel_ms = launch_ms / launches_per_step
     achieved_gbs = bytes_per_launch / (kernel_ms * 1e-3) / 1e9
     value = dist.sum(units_per_step) * args.steps / (max_ms * 1e-3)
     state_gbs_total = dist.sum(bytes_per_launch * launches_per_step * args.steps / (total_ms * 1e-3) / 1e9)
@@ -396,7 +428,7 @@ def run_ours(args, dist: Dist) -> dict | None:
         },
         "e2e": e2e,
         "cpu_baseline": cpu,
-        "gpu_launches": launches_per_step * args.steps,
+        "gpu_launches": kernels_per_step * args.steps,
         "clocks": clocks,
     }
 
@@ -554,6 +586,54 @@ def cpu_baseline(case, seconds: float) -> dict:
     return {"value": w["tokens"] * reps / elapsed, "unit": "tokens/s", "cores": w["threads"], "kind": "port",
             "sample": f"full batch ({w['requests']} sequences, {w['tokens']} tokens) x {reps} repetitions, "
                       f"{elapsed:.1f} s, C oracle with OpenMP"}
+
+
+def unfused_conv_decode_us(case, conv, stream) -> dict | None:
+    """Device time per step of the pipeline conv_decode replaces: vLLM's causal_conv1d_update
+    (Triton) then lightdelta::decode, as vllm_layer.py:199-220 runs them; None without vLLM."""
+    import torch
+
+    try:
+        from vllm.model_executor.layers.mamba.ops.causal_conv1d import causal_conv1d_update
+    except Exception:  # noqa: BLE001
+        return None
+    x = case.qkv.clone()
+    state = conv.state.clone()
+    pool = case.pool.clone()
+    out = torch.empty_like(case.out)
+    slots0 = case.slots[:, 0].contiguous()
+
+    def step():
+        y = causal_conv1d_update(x, state, conv.weight, None, "silu", conv_state_indices=slots0, validate_data=False)
+        torch.ops.lightdelta.decode(y, case.a, case.b, case.a_log, case.dt_bias, case.slots, case.cu, case.accepted,
+                                    pool, case.gate, case.weight, out, 1e-6)
+
+    for _ in range(20):
+        step()
+    torch.cuda.synchronize()
+    begin, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = 500
+    begin.record(stream)
+    for _ in range(steps):
+        step()
+    end.record(stream)
+    torch.cuda.synchronize()
+    vllm_us = begin.elapsed_time(end) * 1000 / steps
+    width = case.slots.shape[1]
+
+    def ours():
+        torch.ops.lightdelta.conv_update(x, state, conv.weight, None, slots0, None, case.cu, width)
+
+    for _ in range(20):
+        ours()
+    torch.cuda.synchronize()
+    begin.record(stream)
+    for _ in range(steps):
+        ours()
+    end.record(stream)
+    torch.cuda.synchronize()
+    return {"us_per_step": vllm_us, "conv_update_alone_us": begin.elapsed_time(end) * 1000 / steps,
+            "pipeline": "vLLM causal_conv1d_update (Triton) + lightdelta::decode, same inputs"}
 
 
 def sampling_cpu_baseline(sampling, seconds: float) -> dict:

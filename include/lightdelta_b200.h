@@ -48,6 +48,7 @@ extern "C" {
 #define LD_FAULT_WAIT_TIMEOUT 0x20u       /* a bounded in-kernel wait expired; that launch's results are incomplete */
 #define LD_FAULT_VERIFY_DRAFTS 0x40u      /* greedy_verify: a request has more drafts than steps */
 #define LD_FAULT_VERIFY_RANGE 0x80u       /* greedy_verify: metadata points outside the logits or token ids */
+#define LD_FAULT_CONV_SLOT_RANGE 0x100u   /* conv update: a conv-state slot index >= n_conv_slots */
 
 /* Head dimension handled by every kernel (K = V). */
 #define LD_HEAD_DIM 128
@@ -156,6 +157,52 @@ int ld_copy_slots(float* pool, int64_t n_pool_slots, int64_t pool_slot_stride,
 #define LD_DECODE_KERNEL_STAGED_Q1 4   /* one CTA per (request, head), TMA-staged state, 3 CTAs/SM */
 #define LD_DECODE_KERNEL_STAGED_Q2 5   /* two-CTA cluster per (request, head), 64 rows each */
 #define LD_DECODE_KERNEL_STAGED_Q4 6   /* four-CTA cluster per (request, head), 32 rows each */
+
+/*
+ * Causal depthwise conv1d state update of the q, k, v channels: vLLM's causal_conv1d_update as
+ * python/lightdelta/integration/vllm_layer.py:161-172 (speculative decode: num_accepted_tokens,
+ * query_start_loc, max_query_len) and :199-207 (one-token decode) call it.  No counterpart in
+ * the reference, which calls vLLM's Triton kernel.
+ *
+ * x: [n_tokens, dim] bf16, rows x_row_stride elements apart; the post-conv activations replace
+ *   the inputs in place (as vLLM does).
+ * conv_state: bf16, element (slot, channel, position) at conv_state[slot * conv_slot_stride +
+ *   channel * conv_dim_stride + position * conv_pos_stride] (vLLM's [slots, dim, L] storage and
+ *   the transposed [slots, L, dim] one are both such views); conv_state_len = L >=
+ *   conv_width - 2 + max_tokens.
+ * conv_weight: [dim, conv_width] bf16 contiguous, 2 <= conv_width <= 4; conv_bias: [dim] bf16 or NULL.
+ * Request r: conv slot slots[r * slots_stride] (0 = the null block: skipped), tokens
+ *   [cu[r], cu[r+1]) (n <= max_tokens), window start accepted[r] - 1 (accepted NULL: 0).
+ *   y_t = silu(bias + sum_j window_j * W[:, j] + x_t * W[:, w-1]) with the window shifting by
+ *   one token per step (fp32 accumulator; bf16 x bf16 products rounded to bf16; y rounded to
+ *   bf16); state positions [0, w - 2) take window positions [o + 1, o + w - 1), then
+ *   [w - 2, w - 2 + n) take the inputs.
+ * A conv slot >= n_conv_slots sets LD_FAULT_CONV_SLOT_RANGE; such requests, requests whose
+ * tokens fall outside [0, n_tokens) (LD_FAULT_DECODE_TOKENS) and requests with accepted outside
+ * [1, max_tokens] are left untouched.
+ */
+int ld_conv_update(void* x, int64_t x_row_stride, int64_t n_tokens, int64_t dim, void* conv_state,
+                   int64_t n_conv_slots, int64_t conv_slot_stride, int64_t conv_dim_stride, int64_t conv_pos_stride,
+                   int64_t conv_state_len, const void* conv_weight, const void* conv_bias, int64_t conv_width,
+                   const int32_t* slots, int64_t slots_stride, const int32_t* accepted, const int32_t* cu,
+                   int64_t n_requests, int64_t max_tokens, void* stream);
+
+/*
+ * The conv update followed by the GDN decode / MTP verify, as the vLLM layer runs them
+ * (vllm_layer.py:161-174, :199-220), in one call: ld_conv_update on qkv with the conv slots
+ * indices[r * width] (vLLM's conv_state_indices = slots[:, 0]), num_accepted_tokens = accepted
+ * and max_tokens = width, then ld_decode on the post-conv qkv.  Arguments as the two; every one
+ * is checked before anything is launched.  No counterpart in the reference.
+ */
+int ld_conv_decode(void* qkv, int64_t qkv_row_stride, const void* a, int64_t a_row_stride, const void* b,
+                   int64_t b_row_stride, const float* a_log, const void* dt_bias, int dt_bias_dtype,
+                   const int32_t* indices, int64_t n_requests, int64_t width, const int32_t* cu,
+                   const int32_t* accepted, float* state, int64_t n_slots, int64_t slot_stride, const void* gate,
+                   int64_t gate_row_stride, const void* weight, int weight_dtype, void* out, int64_t n_tokens,
+                   int64_t num_k_heads, int64_t num_v_heads, float eps, void* conv_state, int64_t n_conv_slots,
+                   int64_t conv_slot_stride, int64_t conv_dim_stride, int64_t conv_pos_stride,
+                   int64_t conv_state_len, const void* conv_weight, const void* conv_bias, int64_t conv_width,
+                   void* stream);
 
 /*
  * Process-wide choice of the kernel that ld_decode launches, for tuning and for testing every

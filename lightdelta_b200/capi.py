@@ -29,6 +29,7 @@ LD_FAULT_COPY_SLOT_RANGE = 0x10
 LD_FAULT_WAIT_TIMEOUT = 0x20
 LD_FAULT_VERIFY_DRAFTS = 0x40
 LD_FAULT_VERIFY_RANGE = 0x80
+LD_FAULT_CONV_SLOT_RANGE = 0x100
 HEAD_DIM = 128
 MAX_WIDTH = 4
 MAX_VERIFY_STEPS = 7
@@ -76,6 +77,13 @@ def lib() -> ctypes.CDLL:
     handle.ld_greedy_verify.restype = i32
     handle.ld_greedy_verify_cluster_override.argtypes = [i32]
     handle.ld_greedy_verify_cluster_override.restype = i32
+    handle.ld_conv_decode.argtypes = [
+        p, i64, p, i64, p, i64, p, p, i32, p, i64, i64, p, p, p, i64, i64, p, i64, p, i32, p, i64, i64, i64, f32,
+        p, i64, i64, i64, i64, i64, p, p, i64, p,
+    ]
+    handle.ld_conv_decode.restype = i32
+    handle.ld_conv_update.argtypes = [p, i64, i64, i64, p, i64, i64, i64, i64, i64, p, p, i64, p, i64, p, p, i64, i64, p]
+    handle.ld_conv_update.restype = i32
     handle.ld_programmatic_launch.argtypes = [i32]
     handle.ld_programmatic_launch.restype = i32
     _lib = handle
@@ -201,4 +209,33 @@ def greedy_verify(logits, cu_num_logits, query_start_loc, input_ids, num_draft_t
         input_ids.numel(), num_draft_tokens.data_ptr(), seq_lens.data_ptr(), prefill_len.data_ptr(),
         num_draft_tokens.numel(), sampled.shape[1] - 1, sampled.data_ptr(), num_sampled.data_ptr(),
         num_rejected.data_ptr(), _stream(logits, stream),
+    ))
+
+
+def conv_decode(qkv, conv_state, conv_weight, conv_bias, a, b, a_log, dt_bias, indices, cu, accepted, state, gate,
+                weight, out, eps=1e-6, stream=None):
+    """ld_conv_decode on torch tensors laid out as torch.ops.lightdelta.conv_decode expects."""
+    hv = state.shape[1]
+    h = (qkv.shape[1] // HEAD_DIM - hv) // 2
+    w = conv_weight.reshape(conv_weight.shape[0], -1)
+    check(lib().ld_conv_decode(
+        qkv.data_ptr(), qkv.stride(0), a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), a_log.data_ptr(),
+        dt_bias.data_ptr(), _dtype_code(dt_bias), indices.data_ptr(), indices.shape[0], indices.shape[1],
+        cu.data_ptr(), accepted.data_ptr(), state.data_ptr(), state.shape[0], state.stride(0), gate.data_ptr(),
+        gate.stride(0), weight.data_ptr(), _dtype_code(weight), out.data_ptr(), qkv.shape[0], h, hv, float(eps),
+        conv_state.data_ptr(), conv_state.shape[0], conv_state.stride(0), conv_state.stride(1), conv_state.stride(2),
+        conv_state.shape[2], w.data_ptr(), None if conv_bias is None else conv_bias.data_ptr(), w.shape[1],
+        _stream(qkv, stream),
+    ))
+
+
+def conv_update(x, conv_state, conv_weight, conv_bias, slots, accepted, cu, max_tokens, stream=None):
+    """ld_conv_update on torch tensors laid out as torch.ops.lightdelta.conv_update expects."""
+    w = conv_weight.reshape(conv_weight.shape[0], -1)
+    check(lib().ld_conv_update(
+        x.data_ptr(), x.stride(0), x.shape[0], x.shape[1], conv_state.data_ptr(), conv_state.shape[0],
+        conv_state.stride(0), conv_state.stride(1), conv_state.stride(2), conv_state.shape[2], w.data_ptr(),
+        None if conv_bias is None else conv_bias.data_ptr(), w.shape[1], slots.data_ptr(), slots.stride(0),
+        None if accepted is None else accepted.data_ptr(), cu.data_ptr(), slots.numel(), int(max_tokens),
+        _stream(x, stream),
     ))

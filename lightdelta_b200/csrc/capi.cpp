@@ -45,13 +45,15 @@ extern "C" int ld_programmatic_launch(int enable) {
 
 extern "C" int ld_fault_flags(uint32_t* flags, int clear) {
   if (flags == nullptr) return ldb::set_error(LD_ERR_INVALID, "ld_fault_flags: flags is NULL");
-  uint32_t decode = 0, state_io = 0, verify = 0;
+  uint32_t decode = 0, state_io = 0, verify = 0, conv = 0;
   int rc = ldb::decode_faults(&decode, clear);
   if (rc != LD_OK) return rc;
   rc = ldb::state_io_faults(&state_io, clear);
   if (rc != LD_OK) return rc;
   rc = ldb::verify_faults(&verify, clear);
   if (rc != LD_OK) return rc;
-  *flags = decode | state_io | verify;
+  rc = ldb::conv_faults(&conv, clear);
+  if (rc != LD_OK) return rc;
+  *flags = decode | state_io | verify | conv;
   return ldb::ok();
 }

@@ -1417,14 +1417,18 @@ int decode_faults(uint32_t* flags, int clear) {
 
 }  // namespace ldb
 
-extern "C" int ld_decode(const void* qkv, int64_t qkv_row_stride, const void* a, int64_t a_row_stride,
-                         const void* b, int64_t b_row_stride, const float* a_log, const void* dt_bias,
-                         int dt_bias_dtype, const int32_t* indices, int64_t n_requests, int64_t width,
-                         const int32_t* cu, const int32_t* accepted, float* state, int64_t n_slots,
-                         int64_t slot_stride, const void* gate, int64_t gate_row_stride,
-                         const void* weight, int weight_dtype, void* out, int64_t n_tokens,
-                         int64_t num_k_heads, int64_t num_v_heads, float eps, void* stream) {
-  using namespace ldb;
+namespace ldb {
+
+// Host-side checks of ld_decode's arguments and the kernel argument block (shared with the
+// fused conv entry point).  args.total_items stays 0 when there is nothing to launch.
+int prepare_decode(const void* qkv, int64_t qkv_row_stride, const void* a, int64_t a_row_stride,
+                   const void* b, int64_t b_row_stride, const float* a_log, const void* dt_bias,
+                   int dt_bias_dtype, const int32_t* indices, int64_t n_requests, int64_t width,
+                   const int32_t* cu, const int32_t* accepted, float* state, int64_t n_slots,
+                   int64_t slot_stride, const void* gate, int64_t gate_row_stride,
+                   const void* weight, int weight_dtype, void* out, int64_t n_tokens,
+                   int64_t num_k_heads, int64_t num_v_heads, float eps, DecodeArgs& args) {
+  args.total_items = 0;
   if (width < 1 || width > LD_MAX_WIDTH) {
     return set_error(LD_ERR_INVALID, "decode/MTP supports 1 through %d tokens per request (got width %lld)",
                      LD_MAX_WIDTH, static_cast<long long>(width));
@@ -1465,7 +1469,6 @@ extern "C" int ld_decode(const void* qkv, int64_t qkv_row_stride, const void* a,
   if (!aligned(state, 16) || slot_stride % 4 != 0) {
     return set_error(LD_ERR_INVALID, "state must be 16-byte aligned with a slot stride divisible by 4");
   }
-  DecodeArgs args;
   args.qkv = static_cast<const __nv_bfloat16*>(qkv);
   args.qkv_row = qkv_row_stride;
   args.a = static_cast<const __nv_bfloat16*>(a);
@@ -1495,6 +1498,25 @@ extern "C" int ld_decode(const void* qkv, int64_t qkv_row_stride, const void* a,
   // K^-1/2 evaluated in double and rounded once, as torch scales an fp32 tensor by a Python float.
   args.q_scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(LD_HEAD_DIM)));
   args.eps = eps;
+  return ok();
+}
+
+}  // namespace ldb
+
+extern "C" int ld_decode(const void* qkv, int64_t qkv_row_stride, const void* a, int64_t a_row_stride,
+                         const void* b, int64_t b_row_stride, const float* a_log, const void* dt_bias,
+                         int dt_bias_dtype, const int32_t* indices, int64_t n_requests, int64_t width,
+                         const int32_t* cu, const int32_t* accepted, float* state, int64_t n_slots,
+                         int64_t slot_stride, const void* gate, int64_t gate_row_stride,
+                         const void* weight, int weight_dtype, void* out, int64_t n_tokens,
+                         int64_t num_k_heads, int64_t num_v_heads, float eps, void* stream) {
+  using namespace ldb;
+  DecodeArgs args;
+  const int rc = prepare_decode(qkv, qkv_row_stride, a, a_row_stride, b, b_row_stride, a_log, dt_bias, dt_bias_dtype,
+                                indices, n_requests, width, cu, accepted, state, n_slots, slot_stride, gate,
+                                gate_row_stride, weight, weight_dtype, out, n_tokens, num_k_heads, num_v_heads, eps,
+                                args);
+  if (rc != LD_OK || args.total_items == 0) return rc;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // TMA bulk copies need 16-byte aligned sources: qkv and gate rows must start on 16 bytes.
@@ -1561,3 +1583,19 @@ extern "C" int ld_decode_kernel_override(int variant) {
   }
   return ldb::g_kernel_override.exchange(variant);
 }
+
+namespace ldb {
+
+int check_decode_args(const void* qkv, int64_t qkv_row_stride, const void* a, int64_t a_row_stride, const void* b,
+                      int64_t b_row_stride, const float* a_log, const void* dt_bias, int dt_bias_dtype,
+                      const int32_t* indices, int64_t n_requests, int64_t width, const int32_t* cu,
+                      const int32_t* accepted, float* state, int64_t n_slots, int64_t slot_stride, const void* gate,
+                      int64_t gate_row_stride, const void* weight, int weight_dtype, void* out, int64_t n_tokens,
+                      int64_t num_k_heads, int64_t num_v_heads, float eps) {
+  DecodeArgs args;
+  return prepare_decode(qkv, qkv_row_stride, a, a_row_stride, b, b_row_stride, a_log, dt_bias, dt_bias_dtype, indices,
+                        n_requests, width, cu, accepted, state, n_slots, slot_stride, gate, gate_row_stride, weight,
+                        weight_dtype, out, n_tokens, num_k_heads, num_v_heads, eps, args);
+}
+
+}  // namespace ldb

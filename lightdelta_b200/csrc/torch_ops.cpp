@@ -26,12 +26,18 @@ void* stream_of(const at::Tensor& t) {
 
 }  // namespace
 
-void decode(const at::Tensor& qkv, const at::Tensor& a, const at::Tensor& b, const at::Tensor& a_log,
-            const at::Tensor& dt_bias, const at::Tensor& indices, const at::Tensor& cu,
-            const at::Tensor& accepted, at::Tensor state, const at::Tensor& gate, const at::Tensor& weight,
-            at::Tensor out, double eps) {
+namespace {
+
+struct DecodeGeometry {
+  int64_t h, hv, n;
+};
+
+// The reference launcher's tensor checks (csrc/gdn_decode.cu:367-403), head counts from the tensors.
+DecodeGeometry check_decode(const at::Tensor& qkv, const at::Tensor& a, const at::Tensor& b, const at::Tensor& a_log,
+                            const at::Tensor& dt_bias, const at::Tensor& indices, const at::Tensor& cu,
+                            const at::Tensor& accepted, const at::Tensor& state, const at::Tensor& gate,
+                            const at::Tensor& weight, const at::Tensor& out, double eps) {
   TORCH_CHECK(qkv.is_cuda() && qkv.scalar_type() == at::kBFloat16, "qkv must be CUDA BF16");
-  const c10::cuda::CUDAGuard guard(qkv.device());
   for (const auto& t : {a, b, gate, out}) {
     TORCH_CHECK(t.device() == qkv.device() && t.scalar_type() == at::kBFloat16 && t.stride(-1) == 1,
                 "activations must be BF16 with dense rows");
@@ -71,13 +77,108 @@ void decode(const at::Tensor& qkv, const at::Tensor& a, const at::Tensor& b, con
                   accepted.numel() == indices.size(0),
               "invalid request metadata shapes");
   TORCH_CHECK(eps > 0, "norm epsilon must be positive");
+  return DecodeGeometry{h, hv, n};
+}
+
+}  // namespace
+
+void decode(const at::Tensor& qkv, const at::Tensor& a, const at::Tensor& b, const at::Tensor& a_log,
+            const at::Tensor& dt_bias, const at::Tensor& indices, const at::Tensor& cu,
+            const at::Tensor& accepted, at::Tensor state, const at::Tensor& gate, const at::Tensor& weight,
+            at::Tensor out, double eps) {
+  TORCH_CHECK(qkv.is_cuda(), "qkv must be CUDA BF16");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  const DecodeGeometry geo = check_decode(qkv, a, b, a_log, dt_bias, indices, cu, accepted, state, gate, weight, out,
+                                          eps);
   if (indices.size(0) == 0) return;
   check_rc(ld_decode(qkv.data_ptr(), qkv.stride(0), a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0),
                      a_log.data_ptr<float>(), dt_bias.data_ptr(), dtype_code(dt_bias),
                      indices.data_ptr<int32_t>(), indices.size(0), indices.size(1), cu.data_ptr<int32_t>(),
                      accepted.data_ptr<int32_t>(), state.data_ptr<float>(), state.size(0), state.stride(0),
                      gate.data_ptr(), gate.stride(0), weight.data_ptr(), dtype_code(weight), out.data_ptr(),
-                     n, h, hv, static_cast<float>(eps), stream_of(qkv)));
+                     geo.n, geo.h, geo.hv, static_cast<float>(eps), stream_of(qkv)));
+}
+
+namespace {
+
+struct ConvTensors {
+  at::Tensor weight;
+  const void* bias;
+};
+
+// Checks of the conv state, weight and bias against a [tokens, dim] activation matrix.
+ConvTensors check_conv(const at::Tensor& x, const at::Tensor& conv_state, const at::Tensor& conv_weight,
+                       const c10::optional<at::Tensor>& conv_bias) {
+  const int64_t dim = x.size(1);
+  TORCH_CHECK(conv_state.device() == x.device() && conv_state.scalar_type() == at::kBFloat16 &&
+                  conv_state.dim() == 3 && conv_state.size(1) == dim,
+              "conv_state must be a CUDA BF16 [slots, dim, L] view");
+  const at::Tensor w = conv_weight.dim() == 3 ? conv_weight.view({conv_weight.size(0), conv_weight.size(2)})
+                                                : conv_weight;
+  TORCH_CHECK(w.device() == x.device() && w.scalar_type() == at::kBFloat16 && w.dim() == 2 && w.size(0) == dim &&
+                  w.is_contiguous(),
+              "conv_weight must be a contiguous CUDA BF16 [dim, width] (or [dim, 1, width]) tensor");
+  const void* bias_ptr = nullptr;
+  if (conv_bias.has_value() && conv_bias->defined()) {
+    TORCH_CHECK(conv_bias->device() == x.device() && conv_bias->scalar_type() == at::kBFloat16 &&
+                    conv_bias->numel() == dim && conv_bias->is_contiguous(),
+                "conv_bias must be a contiguous CUDA BF16 [dim] tensor");
+    bias_ptr = conv_bias->data_ptr();
+  }
+  return ConvTensors{w, bias_ptr};
+}
+
+}  // namespace
+
+// Extension (no reference schema): the causal conv1d state update that produces q, k, v (vLLM's
+// causal_conv1d_update as vllm_layer.py:161-172 and :199-207 call it), in place on x.
+void conv_update(at::Tensor x, at::Tensor conv_state, const at::Tensor& conv_weight,
+                 const c10::optional<at::Tensor>& conv_bias, const at::Tensor& slots,
+                 const c10::optional<at::Tensor>& accepted, const at::Tensor& cu, int64_t max_tokens) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1,
+              "x must be a CUDA BF16 [tokens, dim] matrix with dense rows");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const ConvTensors conv = check_conv(x, conv_state, conv_weight, conv_bias);
+  TORCH_CHECK(slots.device() == x.device() && slots.scalar_type() == at::kInt && slots.dim() == 1,
+              "slots must be a CUDA int32 vector");
+  const int64_t n = slots.numel();
+  TORCH_CHECK(cu.device() == x.device() && cu.scalar_type() == at::kInt && cu.is_contiguous() && cu.numel() == n + 1,
+              "cu must be a contiguous CUDA int32 [requests + 1] vector");
+  const int32_t* accepted_ptr = nullptr;
+  if (accepted.has_value() && accepted->defined()) {
+    TORCH_CHECK(accepted->device() == x.device() && accepted->scalar_type() == at::kInt &&
+                    accepted->is_contiguous() && accepted->numel() == n,
+                "accepted must be a contiguous CUDA int32 [requests] vector");
+    accepted_ptr = accepted->data_ptr<int32_t>();
+  }
+  if (n == 0) return;
+  check_rc(ld_conv_update(x.data_ptr(), x.stride(0), x.size(0), x.size(1), conv_state.data_ptr(), conv_state.size(0),
+                          conv_state.stride(0), conv_state.stride(1), conv_state.stride(2), conv_state.size(2),
+                          conv.weight.data_ptr(), conv.bias, conv.weight.size(1), slots.data_ptr<int32_t>(),
+                          slots.stride(0), accepted_ptr, cu.data_ptr<int32_t>(), n, max_tokens, stream_of(x)));
+}
+
+// Extension (no reference schema): conv update then decode, as vllm_layer.py:161-174 and
+// :199-220 run them; qkv holds the pre-conv activations and receives the post-conv ones.
+void conv_decode(at::Tensor qkv, at::Tensor conv_state, const at::Tensor& conv_weight,
+                 const c10::optional<at::Tensor>& conv_bias, const at::Tensor& a, const at::Tensor& b,
+                 const at::Tensor& a_log, const at::Tensor& dt_bias, const at::Tensor& indices, const at::Tensor& cu,
+                 const at::Tensor& accepted, at::Tensor state, const at::Tensor& gate, const at::Tensor& weight,
+                 at::Tensor out, double eps) {
+  TORCH_CHECK(qkv.is_cuda(), "qkv must be CUDA BF16");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  const DecodeGeometry geo = check_decode(qkv, a, b, a_log, dt_bias, indices, cu, accepted, state, gate, weight, out,
+                                          eps);
+  const ConvTensors conv = check_conv(qkv, conv_state, conv_weight, conv_bias);
+  if (indices.size(0) == 0) return;
+  check_rc(ld_conv_decode(qkv.data_ptr(), qkv.stride(0), a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0),
+                          a_log.data_ptr<float>(), dt_bias.data_ptr(), dtype_code(dt_bias),
+                          indices.data_ptr<int32_t>(), indices.size(0), indices.size(1), cu.data_ptr<int32_t>(),
+                          accepted.data_ptr<int32_t>(), state.data_ptr<float>(), state.size(0), state.stride(0),
+                          gate.data_ptr(), gate.stride(0), weight.data_ptr(), dtype_code(weight), out.data_ptr(),
+                          geo.n, geo.h, geo.hv, static_cast<float>(eps), conv_state.data_ptr(), conv_state.size(0),
+                          conv_state.stride(0), conv_state.stride(1), conv_state.stride(2), conv_state.size(2),
+                          conv.weight.data_ptr(), conv.bias, conv.weight.size(1), stream_of(qkv)));
 }
 
 namespace {
@@ -190,6 +291,13 @@ TORCH_LIBRARY(lightdelta, m) {
   m.def("scatter_state(Tensor packed, Tensor slots, Tensor(p!) pool) -> ()");
   m.def("copy_state(Tensor(p!) pool, Tensor src, Tensor dst) -> ()");
   m.def(
+      "conv_update(Tensor(x!) x, Tensor(c!) conv_state, Tensor conv_weight, Tensor? conv_bias, Tensor slots, "
+      "Tensor? accepted, Tensor cu, int max_tokens) -> ()");
+  m.def(
+      "conv_decode(Tensor(q!) qkv, Tensor(c!) conv_state, Tensor conv_weight, Tensor? conv_bias, Tensor a, Tensor b, "
+      "Tensor a_log, Tensor dt_bias, Tensor indices, Tensor cu, Tensor accepted, Tensor(s!) state, Tensor gate, "
+      "Tensor weight, Tensor(o!) out, float eps) -> ()");
+  m.def(
       "greedy_verify(Tensor logits, Tensor cu_num_logits, Tensor query_start_loc, Tensor input_ids, "
       "Tensor num_draft_tokens, Tensor seq_lens, Tensor prefill_len, Tensor(a!) sampled, "
       "Tensor(b!) num_sampled, Tensor(c!) num_rejected) -> ()");
@@ -201,4 +309,6 @@ TORCH_LIBRARY_IMPL(lightdelta, CUDA, m) {
   m.impl("scatter_state", lightdelta_b200::scatter_state);
   m.impl("copy_state", lightdelta_b200::copy_state);
   m.impl("greedy_verify", lightdelta_b200::greedy_verify);
+  m.impl("conv_decode", lightdelta_b200::conv_decode);
+  m.impl("conv_update", lightdelta_b200::conv_update);
 }

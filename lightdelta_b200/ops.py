@@ -47,3 +47,14 @@ def _copy_fake(pool, src, dst):
 def _greedy_verify_fake(logits, cu_num_logits, query_start_loc, input_ids, num_draft_tokens, seq_lens, prefill_len,
                         sampled, num_sampled, num_rejected):
     return None
+
+
+@torch.library.register_fake("lightdelta::conv_decode")
+def _conv_decode_fake(qkv, conv_state, conv_weight, conv_bias, a, b, a_log, dt_bias, indices, cu, accepted, state,
+                      gate, weight, out, eps):
+    return None
+
+
+@torch.library.register_fake("lightdelta::conv_update")
+def _conv_update_fake(x, conv_state, conv_weight, conv_bias, slots, accepted, cu, max_tokens):
+    return None

@@ -259,3 +259,41 @@ def sampling_case(device, seed: int = 6, requests: int = 64, steps: int = 3, voc
         num_sampled=torch.empty(requests, dtype=torch.int32, device=device),
         num_rejected=torch.empty(requests, dtype=torch.int32, device=device),
     )
+
+
+@dataclass
+class ConvState:
+    """A layer's conv state and conv weights, as vLLM's GDN layer holds them.
+
+    `state` is the [slots, dim, L] view the conv reads ("dim_first": that is the storage;
+    "token_first": a transposed view of [slots, L, dim] storage).  L = width - 2 + max tokens.
+    """
+
+    state: torch.Tensor
+    weight: torch.Tensor
+    bias: torch.Tensor | None
+    storage: torch.Tensor
+
+
+def make_conv_state(case: DecodeCase, slots: int, *, seed: int, conv_width: int = 4, layout: str = "dim_first",
+                    bias: bool = False) -> ConvState:
+    """Seeded bf16 conv state ~ N(0,1), weights ~ 0.5 N(0,1) (and bias ~ 0.1 N(0,1)) for `case`'s
+    qkv width; slot 0 is the null block."""
+    device = case.qkv.device
+    dim = case.qkv.shape[1]
+    width = case.slots.shape[1]
+    length = conv_width - 2 + width
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    shape = (slots, dim, length) if layout == "dim_first" else (slots, length, dim)
+    storage = torch.randn(*shape, device=device, generator=gen).to(torch.bfloat16)
+    view = storage if layout == "dim_first" else storage.transpose(1, 2)
+    weight = (0.5 * torch.randn(dim, conv_width, device=device, generator=gen)).to(torch.bfloat16)
+    b = (0.1 * torch.randn(dim, device=device, generator=gen)).to(torch.bfloat16) if bias else None
+    return ConvState(state=view, weight=weight, bias=b, storage=storage)
+
+
+def conv_decode_args(case: DecodeCase, conv: ConvState) -> tuple:
+    """Arguments of torch.ops.lightdelta.conv_decode (case.qkv holds the pre-conv activations)."""
+    return (case.qkv, conv.state, conv.weight, conv.bias, case.a, case.b, case.a_log, case.dt_bias, case.slots,
+            case.cu, case.accepted, case.pool, case.gate, case.weight, case.out, 1e-6)

@@ -13,6 +13,8 @@ Functions and the reference code they restate:
   scatter_state      csrc/state_io.cu:11-27, :60-69
   copy_slots         python/lightdelta/backend.py:87-91 for states already in the pool
   greedy_verify      python/lightdelta/runtime/speculation.py:274-326 (oracle/greedy_oracle.c)
+  conv_update        vLLM causal_conv1d_update as python/lightdelta/integration/vllm_layer.py:161-172
+                     and :199-207 call it (oracle/conv_oracle.c)
 """
 
 from __future__ import annotations
@@ -36,7 +38,8 @@ def build(force: bool = False) -> Path:
     stale = (
         force
         or not LIB_PATH.exists()
-        or any(p.stat().st_mtime > LIB_PATH.stat().st_mtime for p in (HERE / "gdn_oracle.c", HERE / "greedy_oracle.c", HERE / "Makefile"))
+        or any(p.stat().st_mtime > LIB_PATH.stat().st_mtime for p in (HERE / "gdn_oracle.c", HERE / "greedy_oracle.c", HERE / "conv_oracle.c",
+                                                               HERE / "Makefile"))
     )
     if stale:
         subprocess.run(["make", "-s", "-C", str(HERE)] + (["-B"] if force else []), check=True)
@@ -66,6 +69,9 @@ def lib() -> ctypes.CDLL:
         handle.oracle_argmax_rows.restype = None
         handle.oracle_greedy_verify.argtypes = [p, i32, i64, i64, i64, p, p, p, i64, p, p, p, i64, i64, p, p, p, p, i32]
         handle.oracle_greedy_verify.restype = ctypes.c_uint32
+        handle.oracle_conv_update.argtypes = [p, i64, p, i64, p, i32, i64, i64, i64, i64, i64, p, i32, p, i64, i64,
+                                              p, i64, p, p, i64, i64]
+        handle.oracle_conv_update.restype = i32
         _lib = handle
     return _lib
 
@@ -249,3 +255,39 @@ def greedy_verify(logits, cu_num_logits, query_start_loc, input_ids, num_draft_t
         num_speculative_steps, _ptr(sampled), _ptr(num_sampled), _ptr(num_rejected), _ptr(target), threads,
     )
     return sampled, num_sampled, num_rejected, int(faults)
+
+
+# ---------------------------------------------------------------------------------------------
+# causal conv1d state update (vLLM causal_conv1d_update, vllm_layer.py:161-172, :199-207)
+# ---------------------------------------------------------------------------------------------
+def _elem_code(array: np.ndarray) -> int:
+    if array.dtype == np.float32:
+        return 0
+    if array.dtype == np.uint16:
+        return 1  # bf16 bits
+    raise TypeError(f"unsupported dtype {array.dtype}")
+
+
+def conv_update(x, state, weight, bias, slots, accepted, query_start_loc) -> np.ndarray:
+    """Updates `state` ([slots, dim, L] view, any strides) in place and returns the post-conv
+    activations (same dtype as x / state: float32, or uint16 bf16 bits)."""
+    if x.dtype != state.dtype or x.ndim != 2 or x.strides[1] != x.itemsize:
+        raise TypeError("x must be a matrix of the state dtype with a dense last dimension")
+    if state.ndim != 3:
+        raise TypeError("state must be [slots, dim, L]")
+    weight = np.ascontiguousarray(weight)
+    bias = None if bias is None else np.ascontiguousarray(bias, dtype=weight.dtype)
+    slots, slots_stride = np.ascontiguousarray(slots, dtype=np.int32), 1
+    accepted = _dense(accepted, np.int32)
+    query_start_loc = _dense(query_start_loc, np.int32)
+    y = np.empty(x.shape, x.dtype)
+    item = state.itemsize
+    rc = lib().oracle_conv_update(
+        _ptr(x), x.strides[0] // x.itemsize, _ptr(y), y.shape[1], _ptr(state), _elem_code(state), state.shape[0],
+        state.strides[0] // item, state.strides[1] // item, state.strides[2] // item, state.shape[2], _ptr(weight),
+        _elem_code(weight), _ptr(bias), weight.shape[0], weight.shape[1], _ptr(slots), slots_stride,
+        _ptr(accepted), _ptr(query_start_loc), slots.shape[0], x.shape[0],
+    )
+    if rc != 0:
+        raise ValueError("oracle_conv_update: invalid arguments")
+    return y

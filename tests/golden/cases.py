@@ -59,8 +59,26 @@ SAMPLER_CASES = [
 ]
 
 
+CONV_CASES = [
+    # Speculative decode as vllm_layer.py:161-172 calls it: ragged tokens per request (0..4), a
+    # null conv slot, accepted counts 1..4, bias; state [slots, dim, L] with L = 3 + 3.
+    dict(name="conv_spec_dimfirst", seed=201, requests=10, width=4, max_query_len=4, dim=640, slots=24,
+         layout="dim_first", bias=True, call="spec"),
+    # The same on a token-first state (the transposed view vllm_layer.py:146-147 makes).
+    dict(name="conv_spec_tokenfirst", seed=203, requests=10, width=4, max_query_len=4, dim=640, slots=24,
+         layout="token_first", bias=False, call="spec"),
+    # One-token decode as vllm_layer.py:199-207 calls it (no accepted counts, 2-D x) on a state
+    # sized for speculative decode.
+    dict(name="conv_decode_tokens1", seed=207, requests=12, width=4, max_query_len=1, dim=512, slots=20,
+         layout="dim_first", bias=False, call="decode", state_len=6),
+    # Kernel width 3.
+    dict(name="conv_spec_width3", seed=209, requests=8, width=3, max_query_len=3, dim=384, slots=16,
+         layout="dim_first", bias=True, call="spec"),
+]
+
+
 def spec_by_name(name: str) -> dict:
-    for spec in POST_CONV_CASES + BACKEND_CASES + SAMPLER_CASES:
+    for spec in POST_CONV_CASES + BACKEND_CASES + SAMPLER_CASES + CONV_CASES:
         if spec["name"] == name:
             return spec
     raise KeyError(name)
@@ -218,3 +236,40 @@ def sampler_case(spec: dict) -> dict:
         seq_lens=seq_lens.astype(np.int32),
         prefill_len=prefill_len.astype(np.int32),
     )
+
+
+def conv_case(spec: dict) -> dict:
+    """Inputs of one causal_conv1d_update call (fp32 numpy arrays and int32 metadata).
+
+    state is returned in its storage layout: [slots, dim, L] for "dim_first", [slots, L, dim]
+    for "token_first" (the caller passes the [slots, dim, L] transposed view).
+    """
+    R, W, width, dim, S = (spec[k] for k in ("requests", "max_query_len", "width", "dim", "slots"))
+    L = spec.get("state_len", width - 1 + W - 1)
+    s = spec["seed"] * 100
+    if spec["call"] == "decode":
+        lengths = np.ones(R, np.int64)
+        accepted = np.ones(R, np.int64)
+    else:
+        lengths = detrand.integers(s + 1, R, W + 1)  # 0..W tokens
+        lengths[0] = W
+        accepted = 1 + detrand.integers(s + 2, R, W)
+    qsl = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
+    slots = (1 + np.argsort(detrand.uniform(s + 3, S - 1), kind="stable")[:R]).astype(np.int32)  # distinct
+    if R > 3:
+        slots[3] = 0  # null block: the request is skipped
+    shape = (S, dim, L) if spec["layout"] == "dim_first" else (S, L, dim)
+    return dict(
+        x=detrand.normal(s + 4, (int(qsl[-1]), dim)),
+        state=detrand.normal(s + 5, shape),
+        weight=detrand.normal(s + 6, (dim, width), 0.5),
+        bias=detrand.normal(s + 7, (dim,), 0.1) if spec["bias"] else None,
+        slots=slots,
+        accepted=accepted.astype(np.int32),
+        query_start_loc=qsl,
+    )
+
+
+def conv_state_view(spec: dict, state: np.ndarray) -> np.ndarray:
+    """[slots, dim, L] view of a conv_case state array."""
+    return state if spec["layout"] == "dim_first" else state.transpose(0, 2, 1)

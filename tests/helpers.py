@@ -66,6 +66,42 @@ def assert_state_close(actual: np.ndarray, expected: np.ndarray, what: str = "st
     return float(diff.max()) if diff.size else 0.0
 
 
+# States downstream of a bf16-rounded input (the fused conv's post-conv q, k, v) inherit that
+# input's rounding: where the GPU's and the oracle's exp round one bf16 ulp apart (under 1e-3
+# of post-conv values), the state rows the value touches move by a fraction of that ulp, and
+# over four verify steps the differences compound (measured up to 3.5e-3).  The conv state
+# itself is compared bit-exactly and the outputs with the usual bf16 tolerance.
+CONV_STATE_OUTLIER_FRACTION = 1e-4
+CONV_STATE_OUTLIER_ATOL = 1e-2
+
+
+def assert_out_close_after_conv(actual_bits: np.ndarray, expected_bits: np.ndarray, what: str = "out") -> dict:
+    """Outputs computed from post-conv q, k, v: every element within the reference test's
+    0.008 / 0.02, and at most 1e-3 of them outside 2e-3.  A post-conv q or k value that rounds
+    one ulp apart shifts its whole normalised row, so near-zero outputs can move by a few ulps."""
+    actual = bf16_values(actual_bits).astype(np.float64)
+    expected = bf16_values(expected_bits).astype(np.float64)
+    assert actual.shape == expected.shape, f"{what}: shape {actual.shape} != {expected.shape}"
+    diff = np.abs(actual - expected)
+    ref_ok = diff <= OUT_REF_ATOL + OUT_REF_RTOL * np.abs(expected)
+    assert ref_ok.all(), f"{what}: {int((~ref_ok).sum())} elements outside atol 0.008 / rtol 0.02, max diff {diff.max()}"
+    outliers = diff > NORTH_ATOL + NORTH_RTOL * np.abs(expected)
+    fraction = float(outliers.mean()) if outliers.size else 0.0
+    assert fraction <= MAX_FLIP_FRACTION, f"{what}: {outliers.sum()} elements outside 2e-3 ({fraction:.2e})"
+    return dict(outside_2e3=int(outliers.sum()), max_diff=float(diff.max()) if diff.size else 0.0)
+
+
+def assert_state_close_after_conv(actual: np.ndarray, expected: np.ndarray, what: str = "state") -> dict:
+    actual = np.asarray(actual, dtype=np.float64)
+    expected = np.asarray(expected, dtype=np.float64)
+    diff = np.abs(actual - expected)
+    ok = diff <= STATE_ATOL + STATE_RTOL * np.abs(expected)
+    fraction = float((~ok).mean()) if ok.size else 0.0
+    assert fraction <= CONV_STATE_OUTLIER_FRACTION, f"{what}: {int((~ok).sum())} of {ok.size} outside 3e-6 / 3e-4"
+    assert (diff <= CONV_STATE_OUTLIER_ATOL).all(), f"{what}: max diff {diff.max()} above {CONV_STATE_OUTLIER_ATOL}"
+    return dict(outside=int((~ok).sum()), max_diff=float(diff.max()) if diff.size else 0.0)
+
+
 # ---------------------------------------------------------------------------------------------
 # golden backend cases (H=16, HV=48) as numpy views and as device tensors
 # ---------------------------------------------------------------------------------------------

@@ -57,7 +57,8 @@ def parse_args(argv=None):
     p.add_argument("--steps", type=int, default=4000)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--workload", choices=("decode", "verify", "commit", "sample", "conv", "copy", "stacked"),
+    p.add_argument("--workload", choices=("decode", "verify", "decode_bf16", "verify_bf16", "commit", "sample", "conv",
+                                          "copy", "stacked"),
                    default="decode")
     p.add_argument("--e2e-steps", type=int, default=200)
     p.add_argument("--decode-kernel", choices=("auto", "stream", "rowreg", "tmastore", "staged1", "staged2", "staged4"), default="auto",
@@ -249,6 +250,26 @@ def run_ours(args, dist: Dist) -> dict | None:
                   "sequences_per_gpu": requests, "tokens_per_sequence": width, "num_k_heads": h,
                   "num_v_heads": hv, "head_dim": 128, "pool_slots": case.pool.shape[0],
                   "state_dtype": "fp32", "activation_dtype": "bf16", "decode_kernel": args.decode_kernel}
+    elif args.workload in ("decode_bf16", "verify_bf16"):
+        # The same batches on a bf16 state pool (fp32 recurrence, each stored step rounded).
+        one_token = args.workload == "decode_bf16"
+        case = workloads.config2(device, seed=2 + seed) if one_token else workloads.config3(device, seed=3 + seed)
+        case.pool = case.pool.to(torch.bfloat16)
+        op_args = case.op_args()
+        requests, width = case.slots.shape
+        tokens = case.tokens
+        hv, h = case.num_v_heads, case.num_k_heads
+        bytes_per_launch = workloads.decode_algorithmic_bytes(requests, width, tokens, h, hv, state_itemsize=2)
+        touched = requests * (1 + width) * hv * workloads.SLOT_HEAD_BYTES // 2
+
+        def fn():
+            torch.ops.lightdelta.decode_bf16_state(*op_args)
+
+        units_per_step, unit = tokens, "tokens/s"
+        config = {"workload": f"config{'2' if one_token else '3'}_{args.workload}",
+                  "sequences_per_gpu": requests, "tokens_per_sequence": width, "num_k_heads": h,
+                  "num_v_heads": hv, "head_dim": 128, "pool_slots": case.pool.shape[0],
+                  "state_dtype": "bf16", "activation_dtype": "bf16", "decode_kernel": args.decode_kernel}
     elif args.workload == "commit":
         # Config 3's explicit commit: after verify, copy each sequence's accepted step state to
         # its home slot (the first of its candidate slots) with the pool-to-pool copy op.
@@ -408,7 +429,8 @@ def run_ours(args, dist: Dist) -> dict | None:
         "scaling": "strong" if args.workload == "stacked" else "weak",
         "vs_baseline": None,
         "dtype": {"copy": "fp32 (bit copy)", "commit": "fp32 (bit copy)",
-                  "sample": "fp32 logits, int32 tokens"}.get(args.workload, "fp32"),
+                  "sample": "fp32 logits, int32 tokens", "decode_bf16": "fp32 (bf16 state pool)",
+                  "verify_bf16": "fp32 (bf16 state pool)"}.get(args.workload, "fp32"),
         "data": "synthetic (seeded, BASELINE config shapes and distributions)",
         "impl": "ours",
         "config": {**config, "parallelism": f"slot-sharded x{dist.world}, no collective",

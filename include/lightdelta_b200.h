@@ -159,6 +159,23 @@ int ld_copy_slots(float* pool, int64_t n_pool_slots, int64_t pool_slot_stride,
 #define LD_DECODE_KERNEL_STAGED_Q4 6   /* four-CTA cluster per (request, head), 32 rows each */
 
 /*
+ * ld_decode on a bf16 state pool (state: bf16 [n_slots, HV, 128, 128], slot_stride elements, a
+ * multiple of 8): each request's source state is widened to fp32, updated in fp32 across its
+ * tokens exactly as ld_decode does, and every stored step is rounded to bf16 (nearest even).
+ * Half the state bytes of an fp32 pool per token; results differ from the fp32 pool by that
+ * rounding.  The streaming and one-CTA-per-item kernels run it (ld_decode_kernel_override's
+ * other variants fall back to the automatic choice).  No counterpart in the reference, whose
+ * launcher requires an fp32 pool (csrc/gdn_decode.cu:375-377).
+ */
+int ld_decode_bf16_state(const void* qkv, int64_t qkv_row_stride, const void* a, int64_t a_row_stride,
+                         const void* b, int64_t b_row_stride, const float* a_log, const void* dt_bias,
+                         int dt_bias_dtype, const int32_t* indices, int64_t n_requests, int64_t width,
+                         const int32_t* cu, const int32_t* accepted, void* state, int64_t n_slots,
+                         int64_t slot_stride, const void* gate, int64_t gate_row_stride, const void* weight,
+                         int weight_dtype, void* out, int64_t n_tokens, int64_t num_k_heads, int64_t num_v_heads,
+                         float eps, void* stream);
+
+/*
  * Causal depthwise conv1d state update of the q, k, v channels: vLLM's causal_conv1d_update as
  * python/lightdelta/integration/vllm_layer.py:161-172 (speculative decode: num_accepted_tokens,
  * query_start_loc, max_query_len) and :199-207 (one-token decode) call it.  No counterpart in

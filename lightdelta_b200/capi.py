@@ -63,6 +63,8 @@ def lib() -> ctypes.CDLL:
         p, i64, p, i64, p, i64, p, p, i32, p, i64, i64, p, p, p, i64, i64, p, i64, p, i32, p, i64, i64, i64, f32, p,
     ]
     handle.ld_decode.restype = i32
+    handle.ld_decode_bf16_state.argtypes = handle.ld_decode.argtypes
+    handle.ld_decode_bf16_state.restype = i32
     handle.ld_gather_state.argtypes = [p, i64, i64, p, i64, p, i64, p, i64, i64, p]
     handle.ld_gather_state.restype = i32
     handle.ld_scatter_state.argtypes = [p, i64, p, i64, i64, p, i64, i64, i64, p]
@@ -156,10 +158,14 @@ def _dtype_code(tensor) -> int:
 
 
 def decode(qkv, a, b, a_log, dt_bias, indices, cu, accepted, state, gate, weight, out, eps=1e-6, stream=None):
-    """ld_decode on torch tensors laid out as torch.ops.lightdelta.decode expects."""
+    """ld_decode on torch tensors laid out as torch.ops.lightdelta.decode expects; a bf16 `state`
+    pool goes to ld_decode_bf16_state."""
+    import torch
+
     hv = state.shape[1]
     h = (qkv.shape[1] // HEAD_DIM - hv) // 2
-    check(lib().ld_decode(
+    entry = lib().ld_decode_bf16_state if state.dtype == torch.bfloat16 else lib().ld_decode
+    check(entry(
         qkv.data_ptr(), qkv.stride(0), a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), a_log.data_ptr(),
         dt_bias.data_ptr(), _dtype_code(dt_bias), indices.data_ptr(), indices.shape[0], indices.shape[1],
         cu.data_ptr(), accepted.data_ptr(), state.data_ptr(), state.shape[0], state.stride(0), gate.data_ptr(),

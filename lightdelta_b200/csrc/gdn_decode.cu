@@ -73,7 +73,8 @@ struct DecodeArgs {
   const int32_t* indices;
   const int32_t* cu;
   const int32_t* accepted;
-  float* state;
+  float* state;                  // fp32 state pool (null when the pool is bf16)
+  __nv_bfloat16* state_bf16;     // bf16 state pool (ld_decode_bf16_state), else null
   int64_t n_slots;
   int64_t slot_stride;
   const __nv_bfloat16* gate;
@@ -91,6 +92,18 @@ struct DecodeArgs {
   float q_scale;
   float eps;
 };
+
+// The state pool of a launch as the kernel's element type.
+template <typename StateT>
+__device__ __forceinline__ StateT* state_base(const DecodeArgs& p);
+template <>
+__device__ __forceinline__ float* state_base<float>(const DecodeArgs& p) {
+  return p.state;
+}
+template <>
+__device__ __forceinline__ __nv_bfloat16* state_base<__nv_bfloat16>(const DecodeArgs& p) {
+  return p.state_bf16;
+}
 
 // ------------------------------------------------------------------------------------------
 // scalar helpers
@@ -250,6 +263,51 @@ __device__ __forceinline__ void load_tile(const float* head, int g, int j, float
   }
 }
 
+// bf16 state pools: the same tile, four bf16 values (8 bytes) per float4, widened exactly on load
+// and rounded to nearest-even on store.
+template <int kRows>
+__device__ __forceinline__ void load_tile(const __nv_bfloat16* head, int g, int j, float4 (&s)[kRows][kVecPerRow]) {
+  const uint2* ptr = reinterpret_cast<const uint2*>(head + g * kDim + 4 * j);
+#pragma unroll
+  for (int i = 0; i < kRows; ++i) {
+#pragma unroll
+    for (int c = 0; c < kVecPerRow; ++c) {
+      const uint2 raw = ptr[(i * Tile<kRows>::kRowGroups * kDim + c * 4 * kLanesPerRow) / 4];
+      s[i][c] = make_float4(__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xffff0000u),
+                            __uint_as_float(raw.y << 16), __uint_as_float(raw.y & 0xffff0000u));
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+template <int kRows, int kFirst>
+__device__ __forceinline__ void store_rows_from(uint2* ptr, const float4 (&s)[kRows][kVecPerRow]) {
+#pragma unroll
+  for (int step = 0; step < kRows; ++step) {
+    const int i = (step + kFirst) % kRows;
+#pragma unroll
+    for (int c = 0; c < kVecPerRow; ++c) {
+      ptr[(i * Tile<kRows>::kRowGroups * kDim + c * 4 * kLanesPerRow) / 4] =
+          make_uint2(pack_bf16x2(s[i][c].x, s[i][c].y), pack_bf16x2(s[i][c].z, s[i][c].w));
+    }
+  }
+}
+
+template <int kRows>
+__device__ __forceinline__ void store_tile(__nv_bfloat16* dst_head, int g, int j, const float4 (&s)[kRows][kVecPerRow]) {
+  uint2* ptr = reinterpret_cast<uint2*>(dst_head + g * kDim + 4 * j);
+  switch (blockIdx.x % kRows) {
+    case 0: store_rows_from<kRows, 0>(ptr, s); break;
+    case 1: store_rows_from<kRows, 1 % kRows>(ptr, s); break;
+    case 2: store_rows_from<kRows, 2 % kRows>(ptr, s); break;
+    default: store_rows_from<kRows, 3 % kRows>(ptr, s); break;
+  }
+}
+
 // Gated RMSNorm of one token's 128 recurrence outputs (already bf16-rounded), gdn.py:117-119:
 // out = bf16(o * rsqrt(mean(o^2) + eps) * w * silu(z)).  One warp, 4 values per lane.
 template <bool kVec>
@@ -276,7 +334,7 @@ __device__ __forceinline__ void gated_rmsnorm_store(const float* o_row, const fl
 // ==========================================================================================
 // Fallback kernel: one CTA per item, state loaded straight into registers.
 // ==========================================================================================
-template <bool kVecAct>
+template <bool kVecAct, typename StateT>
 __global__ void __launch_bounds__(Tile<4>::kThreads, 2) gdn_decode_rowreg_kernel(const DecodeArgs p) {
   ldb::grid_dependency_wait();
   ldb::allow_dependent_launch();
@@ -328,7 +386,7 @@ __global__ void __launch_bounds__(Tile<4>::kThreads, 2) gdn_decode_rowreg_kernel
   const int g = tid / kLanesPerRow;
   const int64_t head_offset = static_cast<int64_t>(head) * kHeadElems;
   float4 s[kRows][kVecPerRow];
-  load_tile<kRows>(p.state + static_cast<int64_t>(src) * p.slot_stride + head_offset, g, j, s);
+  load_tile<kRows>(state_base<StateT>(p) + static_cast<int64_t>(src) * p.slot_stride + head_offset, g, j, s);
 
   // Per-token activations: warp t prepares token t.
   if (warp < n) {
@@ -392,7 +450,9 @@ __global__ void __launch_bounds__(Tile<4>::kThreads, 2) gdn_decode_rowreg_kernel
       }
     }
     const int dst = sh_dst[t];
-    if (dst > 0) store_tile<kRows>(p.state + static_cast<int64_t>(dst) * p.slot_stride + head_offset, g, j, s);
+    if (dst > 0) {
+      store_tile<kRows>(state_base<StateT>(p) + static_cast<int64_t>(dst) * p.slot_stride + head_offset, g, j, s);
+    }
   }
   __syncthreads();
 
@@ -413,7 +473,7 @@ __global__ void __launch_bounds__(Tile<4>::kThreads, 2) gdn_decode_rowreg_kernel
 // ==========================================================================================
 namespace stream {
 
-constexpr int kStates = 3;                            // state ring depth (64 KiB each)
+constexpr int kStates = 3;                            // fp32 state ring depth (64 KiB each)
 constexpr int kActs = kStates + 1;                    // activation ring depth
 constexpr uint64_t kWaitLimitNs = 1000000000ull;      // 1 s bound on every mbarrier wait
 
@@ -437,19 +497,26 @@ struct ActStage {
   ItemInfo info;
 };
 
-struct Smem {
-  static constexpr int kStateStages = kStates;
-  static constexpr int kActStages = kActs;
-  float state[kStates][kHeadElems];
-  ActStage act[kActs];
+// State ring of the streaming kernel: three 64 KiB fp32 stages, or six 32 KiB bf16 ones (the same
+// bytes in flight), each with an activation stage behind it.
+template <typename StateT>
+struct SmemT {
+  using State = StateT;
+  static constexpr int kStateStages = sizeof(StateT) == 4 ? kStates : 2 * kStates;
+  static constexpr int kActStages = kStateStages + 1;
+  StateT state[kStateStages][kHeadElems];
+  ActStage act[kActStages];
   float out[2][kMaxTokens][kDim];
-  unsigned long long full[kStates];
-  unsigned long long empty_state[kStates];
-  unsigned long long empty_act[kActs];
+  unsigned long long full[kStateStages];
+  unsigned long long empty_state[kStateStages];
+  unsigned long long empty_act[kActStages];
   unsigned long long out_full[2];   // all consumer warps wrote their rows of out[b]
   unsigned long long out_empty[2];  // all consumer warps are past the epilogue that read out[b]
   int abort;
 };
+using Smem = SmemT<float>;
+static_assert(sizeof(SmemT<float>) <= 227 * 1024 && sizeof(SmemT<__nv_bfloat16>) <= 227 * 1024,
+              "the streaming kernel's ring must fit one CTA's shared memory");
 
 __device__ __forceinline__ uint32_t smem_u32(const void* ptr) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
@@ -633,12 +700,15 @@ __device__ void produce(const DecodeArgs& p, S& sm, int lane) {
       info.n = n;
       info.bos = bos;
       if (kind == kRun) {
-        mbar_arrive_expect_tx(&sm.full[s], kHeadBytes + n * 4 * kRowBytes);
-        const float* src_head = p.state + static_cast<int64_t>(src) * p.slot_stride + static_cast<int64_t>(head) * kHeadElems;
-        // Four 16 KiB pieces, starting at a per-SM quarter (see store_tile).
+        using State = typename S::State;
+        constexpr uint32_t kStateBytes = kHeadElems * sizeof(State);
+        mbar_arrive_expect_tx(&sm.full[s], kStateBytes + n * 4 * kRowBytes);
+        const State* src_head =
+            state_base<State>(p) + static_cast<int64_t>(src) * p.slot_stride + static_cast<int64_t>(head) * kHeadElems;
+        // Four pieces, starting at a per-SM quarter (see store_tile).
         for (int q = 0; q < 4; ++q) {
           const int piece = (q + static_cast<int>(blockIdx.x)) & 3;
-          bulk_load(sm.state[s] + piece * (kHeadElems / 4), src_head + piece * (kHeadElems / 4), kHeadBytes / 4,
+          bulk_load(sm.state[s] + piece * (kHeadElems / 4), src_head + piece * (kHeadElems / 4), kStateBytes / 4,
                     &sm.full[s]);
         }
         const int key_head = head / p.heads_ratio;
@@ -678,8 +748,11 @@ __device__ __forceinline__ void load_row_cols(const __nv_bfloat16* row, int j, f
   }
 }
 
-template <int kRows>
-__device__ void consume(const DecodeArgs& p, Smem& sm, int tid) {
+template <int kRows, class S>
+__device__ void consume(const DecodeArgs& p, S& sm, int tid) {
+  constexpr int kStates = S::kStateStages;
+  constexpr int kActs = S::kActStages;
+  using State = typename S::State;
   constexpr int kConsumers = Tile<kRows>::kThreads;
   constexpr int kRowGroups = Tile<kRows>::kRowGroups;
   const int HV = p.num_v_heads;
@@ -764,7 +837,9 @@ __device__ void consume(const DecodeArgs& p, Smem& sm, int tid) {
         }
       }
       const int dst = info.dst[t];
-      if (dst > 0) store_tile<kRows>(p.state + static_cast<int64_t>(dst) * p.slot_stride + head_offset, g, j, tile);
+      if (dst > 0) {
+        store_tile<kRows>(state_base<State>(p) + static_cast<int64_t>(dst) * p.slot_stride + head_offset, g, j, tile);
+      }
     }
     float z[4] = {0.f, 0.f, 0.f, 0.f};
     if (warp < n) {
@@ -796,14 +871,17 @@ __device__ void consume(const DecodeArgs& p, Smem& sm, int tid) {
 // Block: Tile<kRows>::kThreads consumer threads followed by one producer warp, one CTA per SM.
 // The register cap keeps the block launchable: its 9 warps are spread over the SM's four 16 K-register
 // sub-partitions (at most 3 warps each), which allows 168 registers per thread.
-template <int kRows>
+template <int kRows, typename StateT>
 __global__ void __maxnreg__(168) gdn_decode_stream_kernel(const DecodeArgs p) {
   ldb::grid_dependency_wait();
   ldb::allow_dependent_launch();
   constexpr int kConsumers = Tile<kRows>::kThreads;
   constexpr int kConsumerWarps = kConsumers / 32;
+  using S = SmemT<StateT>;
+  constexpr int kStates = S::kStateStages;
+  constexpr int kActs = S::kActStages;
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+  S& sm = *reinterpret_cast<S*>(smem_raw);
   const int tid = threadIdx.x;
   if (tid == 0) {
     for (int s = 0; s < kStates; ++s) {
@@ -823,7 +901,7 @@ __global__ void __maxnreg__(168) gdn_decode_stream_kernel(const DecodeArgs p) {
   if (tid >= kConsumers) {
     produce(p, sm, tid & 31);
   } else {
-    consume<kRows>(p, sm, tid);
+    consume<kRows, S>(p, sm, tid);
   }
 }
 
@@ -847,6 +925,7 @@ constexpr int kThreads = kConsumers + 64;        // + producer warp + storer war
 // staging tile lets one step's drain overlap the next step's compute.
 template <int kLoads, int kStaging>
 struct Smem {
+  using State = float;
   static constexpr int kStateStages = kLoads;
   static constexpr int kActStages = kLoads + 1;
   float state[kLoads][kHeadElems];
@@ -1362,8 +1441,13 @@ int device_info(DeviceInfo& out) {
   if (!info.stream_ready) {
     err = cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, device);
     if (err != cudaSuccess) return set_error(LD_ERR_CUDA, "SM count: %s", cudaGetErrorString(err));
-    err = cudaFuncSetAttribute(stream::gdn_decode_stream_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    err = cudaFuncSetAttribute(stream::gdn_decode_stream_kernel<4, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(sizeof(stream::Smem)));
+    if (err == cudaSuccess) {
+      err = cudaFuncSetAttribute(stream::gdn_decode_stream_kernel<4, __nv_bfloat16>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(sizeof(stream::SmemT<__nv_bfloat16>)));
+    }
     if (err != cudaSuccess) return set_error(LD_ERR_CUDA, "shared-memory opt-in: %s", cudaGetErrorString(err));
     err = cudaFuncSetAttribute(stream::ts::gdn_decode_tmastore_kernel<2, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(sizeof(stream::ts::Smem<2, 1>)));
@@ -1424,10 +1508,10 @@ namespace ldb {
 int prepare_decode(const void* qkv, int64_t qkv_row_stride, const void* a, int64_t a_row_stride,
                    const void* b, int64_t b_row_stride, const float* a_log, const void* dt_bias,
                    int dt_bias_dtype, const int32_t* indices, int64_t n_requests, int64_t width,
-                   const int32_t* cu, const int32_t* accepted, float* state, int64_t n_slots,
+                   const int32_t* cu, const int32_t* accepted, void* state, int64_t n_slots,
                    int64_t slot_stride, const void* gate, int64_t gate_row_stride,
                    const void* weight, int weight_dtype, void* out, int64_t n_tokens,
-                   int64_t num_k_heads, int64_t num_v_heads, float eps, DecodeArgs& args) {
+                   int64_t num_k_heads, int64_t num_v_heads, float eps, bool state_bf16, DecodeArgs& args) {
   args.total_items = 0;
   if (width < 1 || width > LD_MAX_WIDTH) {
     return set_error(LD_ERR_INVALID, "decode/MTP supports 1 through %d tokens per request (got width %lld)",
@@ -1466,8 +1550,9 @@ int prepare_decode(const void* qkv, int64_t qkv_row_stride, const void* a, int64
     return set_error(LD_ERR_INVALID, "state must hold at least one slot of [HV,128,128] with slot stride >= %lld",
                      static_cast<long long>(slot_elems));
   }
-  if (!aligned(state, 16) || slot_stride % 4 != 0) {
-    return set_error(LD_ERR_INVALID, "state must be 16-byte aligned with a slot stride divisible by 4");
+  if (!aligned(state, 16) || slot_stride % (state_bf16 ? 8 : 4) != 0) {
+    return set_error(LD_ERR_INVALID, "state must be 16-byte aligned with a slot stride divisible by %d",
+                     state_bf16 ? 8 : 4);
   }
   args.qkv = static_cast<const __nv_bfloat16*>(qkv);
   args.qkv_row = qkv_row_stride;
@@ -1480,7 +1565,8 @@ int prepare_decode(const void* qkv, int64_t qkv_row_stride, const void* a, int64
   args.indices = indices;
   args.cu = cu;
   args.accepted = accepted;
-  args.state = state;
+  args.state = state_bf16 ? nullptr : static_cast<float*>(state);
+  args.state_bf16 = state_bf16 ? static_cast<__nv_bfloat16*>(state) : nullptr;
   args.n_slots = n_slots;
   args.slot_stride = slot_stride;
   args.gate = static_cast<const __nv_bfloat16*>(gate);
@@ -1515,7 +1601,7 @@ extern "C" int ld_decode(const void* qkv, int64_t qkv_row_stride, const void* a,
   const int rc = prepare_decode(qkv, qkv_row_stride, a, a_row_stride, b, b_row_stride, a_log, dt_bias, dt_bias_dtype,
                                 indices, n_requests, width, cu, accepted, state, n_slots, slot_stride, gate,
                                 gate_row_stride, weight, weight_dtype, out, n_tokens, num_k_heads, num_v_heads, eps,
-                                args);
+                                false, args);
   if (rc != LD_OK || args.total_items == 0) return rc;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -1558,17 +1644,17 @@ extern "C" int ld_decode(const void* qkv, int64_t qkv_row_stride, const void* a,
                           sizeof(stream::ts::Smem<1, 2>), s, 1, args);
       }
     } else {
-      err = ldb::launch(stream::gdn_decode_stream_kernel<4>, grid, dim3(Tile<4>::kThreads + 32), sizeof(stream::Smem),
-                        s, 1, args);
+      err = ldb::launch(stream::gdn_decode_stream_kernel<4, float>, grid, dim3(Tile<4>::kThreads + 32),
+                        sizeof(stream::Smem), s, 1, args);
     }
   } else {
     const bool vec_act = aligned(qkv, 8) && qkv_row_stride % 4 == 0 && aligned(gate, 8) &&
                          gate_row_stride % 4 == 0 && aligned(out, 8);
     const dim3 grid(static_cast<unsigned int>(args.total_items));
     if (vec_act) {
-      err = ldb::launch(gdn_decode_rowreg_kernel<true>, grid, dim3(Tile<4>::kThreads), 0, s, 1, args);
+      err = ldb::launch(gdn_decode_rowreg_kernel<true, float>, grid, dim3(Tile<4>::kThreads), 0, s, 1, args);
     } else {
-      err = ldb::launch(gdn_decode_rowreg_kernel<false>, grid, dim3(Tile<4>::kThreads), 0, s, 1, args);
+      err = ldb::launch(gdn_decode_rowreg_kernel<false, float>, grid, dim3(Tile<4>::kThreads), 0, s, 1, args);
     }
   }
   if (err != cudaSuccess) {
@@ -1595,7 +1681,49 @@ int check_decode_args(const void* qkv, int64_t qkv_row_stride, const void* a, in
   DecodeArgs args;
   return prepare_decode(qkv, qkv_row_stride, a, a_row_stride, b, b_row_stride, a_log, dt_bias, dt_bias_dtype, indices,
                         n_requests, width, cu, accepted, state, n_slots, slot_stride, gate, gate_row_stride, weight,
-                        weight_dtype, out, n_tokens, num_k_heads, num_v_heads, eps, args);
+                        weight_dtype, out, n_tokens, num_k_heads, num_v_heads, eps, false, args);
 }
 
 }  // namespace ldb
+
+extern "C" int ld_decode_bf16_state(const void* qkv, int64_t qkv_row_stride, const void* a, int64_t a_row_stride,
+                                    const void* b, int64_t b_row_stride, const float* a_log, const void* dt_bias,
+                                    int dt_bias_dtype, const int32_t* indices, int64_t n_requests, int64_t width,
+                                    const int32_t* cu, const int32_t* accepted, void* state, int64_t n_slots,
+                                    int64_t slot_stride, const void* gate, int64_t gate_row_stride,
+                                    const void* weight, int weight_dtype, void* out, int64_t n_tokens,
+                                    int64_t num_k_heads, int64_t num_v_heads, float eps, void* stream) {
+  using namespace ldb;
+  DecodeArgs args;
+  int rc = prepare_decode(qkv, qkv_row_stride, a, a_row_stride, b, b_row_stride, a_log, dt_bias, dt_bias_dtype,
+                          indices, n_requests, width, cu, accepted, state, n_slots, slot_stride, gate, gate_row_stride,
+                          weight, weight_dtype, out, n_tokens, num_k_heads, num_v_heads, eps, true, args);
+  if (rc != LD_OK || args.total_items == 0) return rc;
+  DeviceInfo info;
+  rc = device_info(info);
+  if (rc != LD_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The streaming and one-CTA-per-item kernels have bf16-state forms; the choice follows ld_decode's.
+  const bool bulk_ok = aligned(qkv, 16) && qkv_row_stride % 8 == 0 && aligned(gate, 16) &&
+                       gate_row_stride % 8 == 0 && aligned(out, 8);
+  const int forced = g_kernel_override.load(std::memory_order_relaxed);
+  const bool streaming = bulk_ok && (forced == LD_DECODE_KERNEL_STREAM ||
+                                     (forced != LD_DECODE_KERNEL_ROWREG && width == 1 &&
+                                      args.total_items >= 2 * info.sms));
+  cudaError_t err;
+  if (streaming) {
+    const dim3 grid(static_cast<unsigned int>(std::min<int64_t>(args.total_items, info.sms)));
+    err = ldb::launch(stream::gdn_decode_stream_kernel<4, __nv_bfloat16>, grid, dim3(Tile<4>::kThreads + 32),
+                      sizeof(stream::SmemT<__nv_bfloat16>), s, 1, args);
+  } else {
+    const bool vec_act = aligned(qkv, 8) && qkv_row_stride % 4 == 0 && aligned(gate, 8) &&
+                         gate_row_stride % 4 == 0 && aligned(out, 8);
+    const dim3 grid(static_cast<unsigned int>(args.total_items));
+    err = vec_act ? ldb::launch(gdn_decode_rowreg_kernel<true, __nv_bfloat16>, grid, dim3(Tile<4>::kThreads), 0, s, 1,
+                                args)
+                  : ldb::launch(gdn_decode_rowreg_kernel<false, __nv_bfloat16>, grid, dim3(Tile<4>::kThreads), 0, s,
+                                1, args);
+  }
+  if (err != cudaSuccess) return set_error(LD_ERR_CUDA, "decode launch failed: %s", cudaGetErrorString(err));
+  return ok();
+}

@@ -36,16 +36,18 @@ struct DecodeGeometry {
 DecodeGeometry check_decode(const at::Tensor& qkv, const at::Tensor& a, const at::Tensor& b, const at::Tensor& a_log,
                             const at::Tensor& dt_bias, const at::Tensor& indices, const at::Tensor& cu,
                             const at::Tensor& accepted, const at::Tensor& state, const at::Tensor& gate,
-                            const at::Tensor& weight, const at::Tensor& out, double eps) {
+                            const at::Tensor& weight, const at::Tensor& out, double eps,
+                            at::ScalarType state_type = at::kFloat) {
   TORCH_CHECK(qkv.is_cuda() && qkv.scalar_type() == at::kBFloat16, "qkv must be CUDA BF16");
   for (const auto& t : {a, b, gate, out}) {
     TORCH_CHECK(t.device() == qkv.device() && t.scalar_type() == at::kBFloat16 && t.stride(-1) == 1,
                 "activations must be BF16 with dense rows");
   }
-  for (const auto& t : {a_log, state}) {
-    TORCH_CHECK(t.device() == qkv.device() && t.scalar_type() == at::kFloat && t.stride(-1) == 1,
-                "state and A_log must be CUDA FP32 with dense rows");
-  }
+  TORCH_CHECK(a_log.device() == qkv.device() && a_log.scalar_type() == at::kFloat && a_log.stride(-1) == 1,
+              "state and A_log must be CUDA FP32 with dense rows");
+  TORCH_CHECK(state.device() == qkv.device() && state.scalar_type() == state_type && state.stride(-1) == 1,
+              state_type == at::kFloat ? "state and A_log must be CUDA FP32 with dense rows"
+                                       : "state must be CUDA BF16 with dense rows");
   for (const auto& t : {indices, cu, accepted}) {
     TORCH_CHECK(t.device() == qkv.device() && t.scalar_type() == at::kInt && t.is_contiguous(),
                 "metadata must be contiguous CUDA int32");
@@ -97,6 +99,26 @@ void decode(const at::Tensor& qkv, const at::Tensor& a, const at::Tensor& b, con
                      accepted.data_ptr<int32_t>(), state.data_ptr<float>(), state.size(0), state.stride(0),
                      gate.data_ptr(), gate.stride(0), weight.data_ptr(), dtype_code(weight), out.data_ptr(),
                      geo.n, geo.h, geo.hv, static_cast<float>(eps), stream_of(qkv)));
+}
+
+// Extension (no reference schema): decode on a bf16 state pool, the fp32 recurrence of decode
+// with each stored step rounded to bf16.
+void decode_bf16_state(const at::Tensor& qkv, const at::Tensor& a, const at::Tensor& b, const at::Tensor& a_log,
+                       const at::Tensor& dt_bias, const at::Tensor& indices, const at::Tensor& cu,
+                       const at::Tensor& accepted, at::Tensor state, const at::Tensor& gate,
+                       const at::Tensor& weight, at::Tensor out, double eps) {
+  TORCH_CHECK(qkv.is_cuda(), "qkv must be CUDA BF16");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  const DecodeGeometry geo = check_decode(qkv, a, b, a_log, dt_bias, indices, cu, accepted, state, gate, weight, out,
+                                          eps, at::kBFloat16);
+  if (indices.size(0) == 0) return;
+  check_rc(ld_decode_bf16_state(qkv.data_ptr(), qkv.stride(0), a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0),
+                                a_log.data_ptr<float>(), dt_bias.data_ptr(), dtype_code(dt_bias),
+                                indices.data_ptr<int32_t>(), indices.size(0), indices.size(1),
+                                cu.data_ptr<int32_t>(), accepted.data_ptr<int32_t>(), state.data_ptr(),
+                                state.size(0), state.stride(0), gate.data_ptr(), gate.stride(0), weight.data_ptr(),
+                                dtype_code(weight), out.data_ptr(), geo.n, geo.h, geo.hv, static_cast<float>(eps),
+                                stream_of(qkv)));
 }
 
 namespace {
@@ -287,6 +309,10 @@ TORCH_LIBRARY(lightdelta, m) {
       "decode(Tensor qkv, Tensor a, Tensor b, Tensor a_log, Tensor dt_bias, "
       "Tensor indices, Tensor cu, Tensor accepted, Tensor(s!) state, Tensor gate, "
       "Tensor weight, Tensor(o!) out, float eps) -> ()");
+  m.def(
+      "decode_bf16_state(Tensor qkv, Tensor a, Tensor b, Tensor a_log, Tensor dt_bias, "
+      "Tensor indices, Tensor cu, Tensor accepted, Tensor(s!) state, Tensor gate, "
+      "Tensor weight, Tensor(o!) out, float eps) -> ()");
   m.def("gather_state(Tensor pool, Tensor slots, Tensor valid, Tensor(o!) out) -> ()");
   m.def("scatter_state(Tensor packed, Tensor slots, Tensor(p!) pool) -> ()");
   m.def("copy_state(Tensor(p!) pool, Tensor src, Tensor dst) -> ()");
@@ -305,6 +331,7 @@ TORCH_LIBRARY(lightdelta, m) {
 
 TORCH_LIBRARY_IMPL(lightdelta, CUDA, m) {
   m.impl("decode", lightdelta_b200::decode);
+  m.impl("decode_bf16_state", lightdelta_b200::decode_bf16_state);
   m.impl("gather_state", lightdelta_b200::gather_state);
   m.impl("scatter_state", lightdelta_b200::scatter_state);
   m.impl("copy_state", lightdelta_b200::copy_state);

@@ -28,6 +28,11 @@ def _decode_fake(qkv, a, b, a_log, dt_bias, indices, cu, accepted, state, gate, 
     return None
 
 
+@torch.library.register_fake("lightdelta::decode_bf16_state")
+def _decode_bf16_state_fake(qkv, a, b, a_log, dt_bias, indices, cu, accepted, state, gate, weight, out, eps):
+    return None
+
+
 @torch.library.register_fake("lightdelta::gather_state")
 def _gather_fake(pool, slots, valid, out):
     return None

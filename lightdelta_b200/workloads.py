@@ -72,9 +72,10 @@ def activation_bytes_per_token(num_k_heads: int, num_v_heads: int) -> int:
     return qkv + gate + out + ab
 
 
-def decode_algorithmic_bytes(requests: int, width: int, tokens: int, num_k_heads: int, num_v_heads: int) -> int:
+def decode_algorithmic_bytes(requests: int, width: int, tokens: int, num_k_heads: int, num_v_heads: int,
+                             state_itemsize: int = 4) -> int:
     """State read once per request, written once per step, plus activations."""
-    slot = num_v_heads * SLOT_HEAD_BYTES
+    slot = num_v_heads * SLOT_HEAD_BYTES * state_itemsize // 4
     return requests * (1 + width) * slot + tokens * activation_bytes_per_token(num_k_heads, num_v_heads)
 
 

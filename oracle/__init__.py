@@ -54,11 +54,11 @@ def lib() -> ctypes.CDLL:
         p, i64, i32, f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
         handle.oracle_post_conv_gdn.argtypes = [i64] * 6 + [p] * 11 + [i32, f32, p, p, p, i32]
         handle.oracle_post_conv_gdn.restype = i32
-        handle.oracle_decode.argtypes = [
-            p, i64, p, i64, p, i64, p, p, i32, p, i64, i64, p, p, p, i64, i64, p, i64, p, i32, p, i64, i64, i64,
-            f32, i32,
+        handle.oracle_decode_state.argtypes = [
+            p, i64, p, i64, p, i64, p, p, i32, p, i64, i64, p, p, p, i32, i64, i64, p, i64, p, i32, p, i64, i64,
+            i64, f32, i32,
         ]
-        handle.oracle_decode.restype = i32
+        handle.oracle_decode_state.restype = i32
         handle.oracle_gather_state.argtypes = [p, i64, i64, p, i64, p, i64, p, i64, i64, i32]
         handle.oracle_gather_state.restype = None
         handle.oracle_scatter_state.argtypes = [p, i64, p, i64, i64, p, i64, i64, i64]
@@ -135,16 +135,18 @@ def post_conv_gdn(q, k, v, a, b, a_log, dt_bias, gate, norm_weight, initial_stat
 # ---------------------------------------------------------------------------------------------
 def decode(qkv, a, b, a_log, dt_bias, indices, cu, accepted, state, gate, weight, out, *, num_k_heads: int,
            eps: float = 1e-6, threads: int = 0) -> None:
-    """In-place on `state` (fp32 [S,HV,128,128]) and `out` (uint16 [N,HV,128]).
+    """In-place on `state` ([S,HV,128,128]) and `out` (uint16 [N,HV,128]).
 
     qkv, a, b, gate, out are uint16 (bf16 bits) 2-D/3-D arrays whose last dimension is dense
     (row strides may exceed the row); dt_bias and weight may be float32 or uint16 (bf16).
+    `state` is float32 (the reference's pool) or uint16 bf16 bits (a bf16 pool: fp32 recurrence,
+    each stored step rounded to bf16).
     """
     for name, arr in (("qkv", qkv), ("a", a), ("b", b), ("gate", gate), ("out", out)):
         if arr.dtype != np.uint16 or arr.strides[-1] != 2:
             raise TypeError(f"{name} must be a uint16 (bf16 bits) array with a dense last dimension")
-    if state.dtype != np.float32 or not state[0].flags.c_contiguous:
-        raise TypeError("state must be float32 with dense slots")
+    if state.dtype not in (np.float32, np.uint16) or not state[0].flags.c_contiguous:
+        raise TypeError("state must be float32 or uint16 (bf16 bits) with dense slots")
     if gate.ndim != 3 or gate.strides[1] != HEAD_DIM * 2 or not out.flags.c_contiguous:
         raise TypeError("gate must be [N,HV,128] with head stride 128 and out contiguous")
     indices = _dense(indices, np.int32)
@@ -157,10 +159,10 @@ def decode(qkv, a, b, a_log, dt_bias, indices, cu, accepted, state, gate, weight
     weight = _dense(weight, np.uint16 if weight_bf16 else np.float32)
     R, W = indices.shape
     S, HV = state.shape[0], state.shape[1]
-    rc = lib().oracle_decode(
+    rc = lib().oracle_decode_state(
         _ptr(qkv), qkv.strides[0] // 2, _ptr(a), a.strides[0] // 2, _ptr(b), b.strides[0] // 2, _ptr(a_log),
-        _ptr(dt_bias), int(dt_bias_bf16), _ptr(indices), R, W, _ptr(cu), _ptr(accepted), _ptr(state), S,
-        state.strides[0] // 4, _ptr(gate), gate.strides[0] // 2, _ptr(weight), int(weight_bf16), _ptr(out),
+        _ptr(dt_bias), int(dt_bias_bf16), _ptr(indices), R, W, _ptr(cu), _ptr(accepted), _ptr(state),
+        int(state.dtype == np.uint16), S, state.strides[0] // state.itemsize, _ptr(gate), gate.strides[0] // 2, _ptr(weight), int(weight_bf16), _ptr(out),
         qkv.shape[0], num_k_heads, HV, eps, threads,
     )
     if rc != 0:

@@ -171,13 +171,35 @@ int oracle_post_conv_gdn(int64_t B, int64_t T, int64_t Hk, int64_t Hv, int64_t K
  *   source = indices[r*W + accepted[r]-1]; step t's state -> indices[r*W+t] if > 0.
  * Invalid requests (no valid source, n > W, source >= n_slots) get zero outputs and no
  * writes; a request with no tokens is skipped (gdn_decode.cu:150-168).
+ * state_bf16 selects a bf16 pool (no counterpart in the reference, whose pool is fp32): the
+ * source head is widened to fp32, the recurrence runs in fp32 across the request's tokens, and
+ * each stored step is rounded to bf16 (nearest even).
  * Returns 0, or -1 on invalid arguments.
  */
-int oracle_decode(const uint16_t* qkv, int64_t qkv_row, const uint16_t* a, int64_t a_row, const uint16_t* b,
-                  int64_t b_row, const float* a_log, const void* dt_bias, int dt_bias_bf16, const int32_t* indices,
-                  int64_t R, int64_t W, const int32_t* cu, const int32_t* accepted, float* state, int64_t n_slots,
-                  int64_t slot_stride, const uint16_t* gate, int64_t gate_row, const void* weight, int weight_bf16,
-                  uint16_t* out, int64_t n_tokens, int64_t H, int64_t HV, float eps, int threads) {
+static void load_head(const void* state, int state_bf16, int64_t at, float* S, int64_t n) {
+  if (!state_bf16) {
+    memcpy(S, (const float*)state + at, sizeof(float) * (size_t)n);
+    return;
+  }
+  const uint16_t* src = (const uint16_t*)state + at;
+  for (int64_t i = 0; i < n; ++i) S[i] = bf16_to_f32(src[i]);
+}
+
+static void store_head(void* state, int state_bf16, int64_t at, const float* S, int64_t n) {
+  if (!state_bf16) {
+    memcpy((float*)state + at, S, sizeof(float) * (size_t)n);
+    return;
+  }
+  uint16_t* dst = (uint16_t*)state + at;
+  for (int64_t i = 0; i < n; ++i) dst[i] = f32_to_bf16(S[i]);
+}
+
+int oracle_decode_state(const uint16_t* qkv, int64_t qkv_row, const uint16_t* a, int64_t a_row, const uint16_t* b,
+                        int64_t b_row, const float* a_log, const void* dt_bias, int dt_bias_bf16,
+                        const int32_t* indices, int64_t R, int64_t W, const int32_t* cu, const int32_t* accepted,
+                        void* state, int state_bf16, int64_t n_slots, int64_t slot_stride, const uint16_t* gate,
+                        int64_t gate_row, const void* weight, int weight_bf16, uint16_t* out, int64_t n_tokens,
+                        int64_t H, int64_t HV, float eps, int threads) {
   const int64_t D = ORACLE_DIM;
   if (W < 1 || W > 4 || H <= 0 || HV <= 0 || HV % H != 0 || !(eps > 0.0f)) return -1;
   const int64_t ratio = HV / H;
@@ -203,7 +225,7 @@ int oracle_decode(const uint16_t* qkv, int64_t qkv_row, const uint16_t* a, int64
     float* S = (float*)malloc(sizeof(float) * (size_t)(head_elems + 6 * D));
     float *qn = S + head_elems, *kn = qn + D, *vv = kn + D, *z = vv + D, *raw = z + D, *out_row = raw + D;
     float scratch[ORACLE_DIM];
-    memcpy(S, state + src * slot_stride + h * head_elems, sizeof(float) * (size_t)head_elems);
+    load_head(state, state_bf16, src * slot_stride + h * head_elems, S, head_elems);
     const float g_scale = -expf(a_log[h]);
     const float dt = dt_bias_bf16 ? bf16_to_f32(((const uint16_t*)dt_bias)[h]) : ((const float*)dt_bias)[h];
     for (int64_t t = 0; t < n; ++t) {
@@ -224,12 +246,22 @@ int oracle_decode(const uint16_t* qkv, int64_t qkv_row, const uint16_t* a, int64
       for (int64_t i = 0; i < D; ++i) out[(token * HV + h) * D + i] = f32_to_bf16(out_row[i]);
       const int64_t dst = indices[r * W + t];
       if (dst > 0 && dst < n_slots) {
-        memcpy(state + dst * slot_stride + h * head_elems, S, sizeof(float) * (size_t)head_elems);
+        store_head(state, state_bf16, dst * slot_stride + h * head_elems, S, head_elems);
       }
     }
     free(S);
   }
   return 0;
+}
+
+int oracle_decode(const uint16_t* qkv, int64_t qkv_row, const uint16_t* a, int64_t a_row, const uint16_t* b,
+                  int64_t b_row, const float* a_log, const void* dt_bias, int dt_bias_bf16, const int32_t* indices,
+                  int64_t R, int64_t W, const int32_t* cu, const int32_t* accepted, float* state, int64_t n_slots,
+                  int64_t slot_stride, const uint16_t* gate, int64_t gate_row, const void* weight, int weight_bf16,
+                  uint16_t* out, int64_t n_tokens, int64_t H, int64_t HV, float eps, int threads) {
+  return oracle_decode_state(qkv, qkv_row, a, a_row, b, b_row, a_log, dt_bias, dt_bias_bf16, indices, R, W, cu,
+                             accepted, state, 0, n_slots, slot_stride, gate, gate_row, weight, weight_bf16, out,
+                             n_tokens, H, HV, eps, threads);
 }
 
 /* gather_state (csrc/state_io.cu:11-27, :44-58): out[i] = live ? pool[slot] : 0. */

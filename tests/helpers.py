@@ -57,6 +57,36 @@ def assert_out_close(actual_bits: np.ndarray, expected_bits: np.ndarray, what: s
                 outside_2e3=int(outliers.sum()), max_diff=float(diff.max()) if diff.size else 0.0)
 
 
+# A bf16 state pool: the device and the oracle both run the recurrence in fp32 and round each
+# stored step to bf16, so their fp32 values (within 3e-6 / 3e-4 of each other) round to the same
+# bf16 value except where they straddle a rounding boundary (one ulp apart) or where a value
+# near zero has bf16 ulps finer than the fp32 tolerance (then the fp32 tolerance applies).
+BF16_STATE_MAX_FLIP_FRACTION = 1e-2
+
+
+def assert_bf16_state_close(actual_bits: np.ndarray, expected_bits: np.ndarray, what: str = "bf16 state",
+                            max_ulps: int = 1) -> dict:
+    """max_ulps: 1 for states one launch stored from the same source; k after k chained launches,
+    each re-reading the previous launch's rounded state.  A flip in one launch feeds the next:
+    S' = decay * S + k * delta moves by up to decay times the flipped element's ulp, and where S'
+    cancels to near zero that absolute change is many of its own ulps, so chained launches also
+    allow (k - 1) ulps of the largest state magnitude as an absolute difference."""
+    ulps = bf16_ulp_distance(actual_bits, expected_bits)
+    actual = bf16_values(actual_bits).astype(np.float64)
+    expected = bf16_values(expected_bits).astype(np.float64)
+    diff = np.abs(actual - expected)
+    chain_atol = (max_ulps - 1) * 2.0 ** -8 * (float(np.abs(expected).max()) if expected.size else 0.0)
+    ok = (ulps <= max_ulps) | (diff <= STATE_ATOL + STATE_RTOL * np.abs(expected)) | (diff <= chain_atol)
+    if not ok.all():
+        worst = [(float(actual[tuple(i)]), float(expected[tuple(i)])) for i in np.argwhere(~ok)[:4]]
+        raise AssertionError(f"{what}: {int((~ok).sum())} elements more than {max_ulps} bf16 ulps and "
+                             f"3e-6 / 3e-4 apart (actual, expected): {worst}")
+    fraction = float((ulps >= 1).mean()) if ulps.size else 0.0
+    assert fraction <= BF16_STATE_MAX_FLIP_FRACTION, f"{what}: {int((ulps >= 1).sum())} differ ({fraction:.2e})"
+    return dict(elements=int(ulps.size), one_ulp=int((ulps == 1).sum()), more=int((ulps > 1).sum()),
+                max_diff=float(diff.max()) if diff.size else 0.0)
+
+
 def assert_state_close(actual: np.ndarray, expected: np.ndarray, what: str = "state") -> float:
     actual = np.asarray(actual, dtype=np.float64)
     expected = np.asarray(expected, dtype=np.float64)
@@ -79,6 +109,14 @@ def assert_out_close_after_conv(actual_bits: np.ndarray, expected_bits: np.ndarr
     """Outputs computed from post-conv q, k, v: every element within the reference test's
     0.008 / 0.02, and at most 1e-3 of them outside 2e-3.  A post-conv q or k value that rounds
     one ulp apart shifts its whole normalised row, so near-zero outputs can move by a few ulps."""
+    return assert_out_close_tail(actual_bits, expected_bits, what)
+
+
+def assert_out_close_tail(actual_bits: np.ndarray, expected_bits: np.ndarray, what: str = "out") -> dict:
+    """Every element within the reference test's 0.008 / 0.02 and at most 1e-3 of them outside
+    2e-3, without the one-ulp bound on those few: for inputs whose recurrence outputs sit near a
+    bf16 rounding boundary (the output is rounded to bf16 before the gated RMSNorm), a one-ulp
+    flip there is scaled by the norm and can land two ulps apart after the final rounding."""
     actual = bf16_values(actual_bits).astype(np.float64)
     expected = bf16_values(expected_bits).astype(np.float64)
     assert actual.shape == expected.shape, f"{what}: shape {actual.shape} != {expected.shape}"
@@ -163,7 +201,8 @@ def to_numpy_case(kwargs: dict) -> dict:
         slots=kwargs["slots"].cpu().numpy(),
         cu=kwargs["cu"].cpu().numpy(),
         accepted=kwargs["accepted"].cpu().numpy(),
-        pool=kwargs["pool"].cpu().numpy(),
+        pool=(host_bf16(kwargs["pool"]).copy() if kwargs["pool"].dtype == torch.bfloat16
+              else kwargs["pool"].cpu().numpy()),
         gate=host_bf16(kwargs["gate"]),
         weight=(host_bf16(kwargs["weight"]) if kwargs["weight"].dtype == torch.bfloat16
                 else kwargs["weight"].cpu().numpy()),

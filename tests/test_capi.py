@@ -75,6 +75,16 @@ def test_decode_rejects_null_pointers(native):
     assert "NULL" in native.last_error()
 
 
+def test_bf16_state_pool_needs_a_slot_stride_divisible_by_8(native):
+    """Host-side checks only: the addresses are never dereferenced (the call fails validation)."""
+    fake = 1 << 20  # 16-byte aligned, non-NULL
+    slot = 48 * 128 * 128
+    args = [fake, 10240, fake, 48, fake, 48, fake, fake, 0, fake, 4, 1, fake, fake, fake, 2, slot + 4, fake, 6144,
+            fake, 0, fake, 4, 16, 48, 1e-6, None]
+    assert native.lib().ld_decode_bf16_state(*args) == native.LD_ERR_INVALID
+    assert "divisible by 8" in native.last_error()
+
+
 def test_state_io_validation(native):
     lib = native.lib()
     assert lib.ld_gather_state(None, 4, 16, None, 1, None, 0, None, 16, 16, None) == native.LD_OK

@@ -133,3 +133,22 @@ def test_oracle_decode_invalid_requests_write_nothing():
     assert np.count_nonzero(x["out"][:6]) == 0
     assert (bf16_values(x["out"][6:]) == 1.0).all()
     np.testing.assert_array_equal(x["pool"], before)
+
+
+@pytest.mark.parametrize("name", [c["name"] for c in cases.BACKEND_CASES])
+def test_oracle_bf16_pool_is_the_fp32_recurrence_rounded_per_step(name):
+    """The bf16-pool mode, pinned to the fp32 mode (itself pinned to the reference): from a pool
+    of bf16 values it gives the same outputs as the fp32 pool holding those values widened, and
+    stores each step's fp32 state rounded to bf16 (nearest even)."""
+    spec = cases.spec_by_name(name)
+    x = backend_numpy(spec)
+    pool_bits = detrand.bf16_bits(x["pool"])
+    x["pool"] = bf16_values(pool_bits)
+    y = dict(x, pool=pool_bits.copy(), out=np.zeros_like(x["out"]))
+    for args in (x, y):
+        oracle.decode(args["qkv"], args["a"], args["b"], args["a_log"], args["dt_bias"], args["slots"], args["cu"],
+                      args["accepted"], args["pool"], args["gate"], args["weight"], args["out"],
+                      num_k_heads=args["num_k_heads"])
+    np.testing.assert_array_equal(y["out"], x["out"])
+    np.testing.assert_array_equal(y["pool"], detrand.bf16_bits(x["pool"]))
+    assert not np.array_equal(y["pool"], pool_bits)  # some slots were written

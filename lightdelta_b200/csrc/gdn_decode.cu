@@ -173,53 +173,77 @@ __device__ __forceinline__ void token_gates(const DecodeArgs& p, int64_t token, 
   beta = 1.0f / (1.0f + expf(-b_val));
 }
 
+// Paired fp32 arithmetic (sm_100's f32x2 forms): two independent IEEE fp32 operations per
+// instruction, each lane rounded exactly as the scalar instruction would round it.
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 lo2(const float4& v) { return make_float2(v.x, v.y); }
+__device__ __forceinline__ float2 hi2(const float4& v) { return make_float2(v.z, v.w); }
+
 // One delta-rule step on the register tile (gdn.py:111-114), then o = S q for the tile's rows
 // (gdn.py:115), reduced over the row group.  kv / qv are this lane's normalised k and q columns.
+// The decay and the rank-1 update are element-wise (paired instructions, same rounding as the
+// scalar form); each lane's partial dot products keep four partial sums (the .x/.y lanes of the
+// low and high column pairs), added at the end.
 template <int kRows>
 __device__ __forceinline__ void tile_step(float4 (&s)[kRows][kVecPerRow], const float4 (&kv)[kVecPerRow],
                                           const float4 (&qv)[kVecPerRow], const float (&vrow)[kRows],
                                           float decay, float beta, float (&o)[kRows]) {
+  const float2 decay2 = make_float2(decay, decay);
   float pred[kRows];
 #pragma unroll
   for (int i = 0; i < kRows; ++i) {
-    float acc = 0.0f;
+    float2 acc_lo = make_float2(0.0f, 0.0f), acc_hi = make_float2(0.0f, 0.0f);
 #pragma unroll
     for (int c = 0; c < kVecPerRow; ++c) {
-      s[i][c].x *= decay;
-      s[i][c].y *= decay;
-      s[i][c].z *= decay;
-      s[i][c].w *= decay;
-      acc = fmaf(s[i][c].x, kv[c].x, acc);
-      acc = fmaf(s[i][c].y, kv[c].y, acc);
-      acc = fmaf(s[i][c].z, kv[c].z, acc);
-      acc = fmaf(s[i][c].w, kv[c].w, acc);
+      const float2 lo = mul2(lo2(s[i][c]), decay2);
+      const float2 hi = mul2(hi2(s[i][c]), decay2);
+      s[i][c] = make_float4(lo.x, lo.y, hi.x, hi.y);
+      acc_lo = fma2(lo, lo2(kv[c]), acc_lo);
+      acc_hi = fma2(hi, hi2(kv[c]), acc_hi);
     }
-    pred[i] = acc;
+    pred[i] = (acc_lo.x + acc_lo.y) + (acc_hi.x + acc_hi.y);
   }
 #pragma unroll
   for (int i = 0; i < kRows; ++i) pred[i] = row_sum(pred[i]);
 #pragma unroll
   for (int i = 0; i < kRows; ++i) {
     const float delta = (vrow[i] - pred[i]) * beta;
+    const float2 delta2 = make_float2(delta, delta);
 #pragma unroll
     for (int c = 0; c < kVecPerRow; ++c) {
-      s[i][c].x = fmaf(delta, kv[c].x, s[i][c].x);
-      s[i][c].y = fmaf(delta, kv[c].y, s[i][c].y);
-      s[i][c].z = fmaf(delta, kv[c].z, s[i][c].z);
-      s[i][c].w = fmaf(delta, kv[c].w, s[i][c].w);
+      const float2 lo = fma2(lo2(kv[c]), delta2, lo2(s[i][c]));
+      const float2 hi = fma2(hi2(kv[c]), delta2, hi2(s[i][c]));
+      s[i][c] = make_float4(lo.x, lo.y, hi.x, hi.y);
     }
   }
 #pragma unroll
   for (int i = 0; i < kRows; ++i) {
-    float acc = 0.0f;
+    float2 acc_lo = make_float2(0.0f, 0.0f), acc_hi = make_float2(0.0f, 0.0f);
 #pragma unroll
     for (int c = 0; c < kVecPerRow; ++c) {
-      acc = fmaf(s[i][c].x, qv[c].x, acc);
-      acc = fmaf(s[i][c].y, qv[c].y, acc);
-      acc = fmaf(s[i][c].z, qv[c].z, acc);
-      acc = fmaf(s[i][c].w, qv[c].w, acc);
+      acc_lo = fma2(lo2(s[i][c]), lo2(qv[c]), acc_lo);
+      acc_hi = fma2(hi2(s[i][c]), hi2(qv[c]), acc_hi);
     }
-    o[i] = acc;
+    o[i] = (acc_lo.x + acc_lo.y) + (acc_hi.x + acc_hi.y);
   }
 #pragma unroll
   for (int i = 0; i < kRows; ++i) o[i] = row_sum(o[i]);
@@ -754,17 +778,16 @@ __device__ void consume(const DecodeArgs& p, S& sm, int tid) {
   constexpr int kActs = S::kActStages;
   using State = typename S::State;
   constexpr int kConsumers = Tile<kRows>::kThreads;
+  constexpr int kConsumerWarps = kConsumers / 32;
   constexpr int kRowGroups = Tile<kRows>::kRowGroups;
   const int HV = p.num_v_heads;
   const int lane = tid & 31;
   const int warp = tid >> 5;
   const int j = tid & (kLanesPerRow - 1);
   const int g = tid / kLanesPerRow;
-  float w[4] = {0.f, 0.f, 0.f, 0.f};
-  if (warp < kMaxTokens) {
+  float w[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) w[e] = load_param(p.weight, 4 * lane + e, p.weight_bf16);
-  }
+  for (int e = 0; e < 4; ++e) w[e] = load_param(p.weight, 4 * lane + e, p.weight_bf16);
   int k = 0;
   int runs = 0;
   for (int64_t item = blockIdx.x; item < p.total_items; item += gridDim.x, ++k) {
@@ -841,9 +864,16 @@ __device__ void consume(const DecodeArgs& p, S& sm, int tid) {
         store_tile<kRows>(state_base<State>(p) + static_cast<int64_t>(dst) * p.slot_stride + head_offset, g, j, tile);
       }
     }
+    // Token et's gated RMSNorm runs on warp et, or with a bf16 pool on warp (runs + et) mod
+    // kConsumerWarps, moving round the warps from item to item.  Measured on B200 (config 2,
+    // 256 x T=1, HV=32): rotating takes the bf16 pool from 141.9 to 132.1 us, where the compute
+    // per item is the bound and warp 0 was the slowest; with the HBM-bound fp32 pool it costs
+    // 175 -> 192 us, so the fp32 pool keeps the fixed assignment.
+    constexpr bool kRotateEpilogue = sizeof(State) == 2;
+    const int et = kRotateEpilogue ? (warp + kConsumerWarps - runs % kConsumerWarps) % kConsumerWarps : warp;
     float z[4] = {0.f, 0.f, 0.f, 0.f};
-    if (warp < n) {
-      const uint2 raw = *reinterpret_cast<const uint2*>(&act.z[warp][4 * lane]);
+    if (et < n) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(&act.z[et][4 * lane]);
       z[0] = bf16_lo(raw.x);
       z[1] = bf16_hi(raw.x);
       z[2] = bf16_lo(raw.y);
@@ -854,13 +884,12 @@ __device__ void consume(const DecodeArgs& p, S& sm, int tid) {
       mbar_arrive(&sm.empty_act[a]);
       mbar_arrive(&sm.out_full[buf]);
     }
-    if (warp < n) {
+    if (et < n) {
       if (!warp_wait(&sm.out_full[buf], use & 1)) {  // every row's output of this item is in o_buf
         if (lane == 0) set_abort(sm);
         break;
       }
-      gated_rmsnorm_store<true>(o_buf + warp * kDim, z, w, p.eps, lane,
-                                p.out + ((bos + warp) * HV + head) * kDim);
+      gated_rmsnorm_store<true>(o_buf + et * kDim, z, w, p.eps, lane, p.out + ((bos + et) * HV + head) * kDim);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.out_empty[buf]);

@@ -16,7 +16,7 @@
 // {32c + 4j .. 32c + 4j + 3 : c = 0..3}, so each warp-wide 128-bit access touches four fully
 // used 128-byte lines, and the row dot products S k and S q reduce with three xor-shuffles.
 //
-// gdn_decode_stream_kernel (default): persistent, one CTA per SM.  A producer warp streams the
+// gdn_decode_stream_kernel (large one-token launches): persistent, one CTA per SM.  A producer warp streams the
 // states of the CTA's items into a 3-deep shared-memory ring with TMA bulk copies
 // (cp.async.bulk, completion on an mbarrier) together with the items' q/k/v/gate rows, while
 // 8 consumer warps run the recurrence on the register tile and store each step's state
@@ -25,9 +25,13 @@
 // (LD_FAULT_WAIT_TIMEOUT).  No cluster and no multicast: each CTA reads only its own items
 // from this GPU's memory.
 //
-// gdn_decode_rowreg_kernel (fallback): one CTA per item, loading the state straight into
-// registers with 128-bit loads.  Used when the activation rows are not 16-byte aligned (TMA
-// bulk copies need 16-byte aligned sources).
+// gdn_decode_rowreg_kernel: one CTA per item, loading the state straight into registers with
+// 128-bit loads.  Used for multi-token verify, for one-token launches below kStreamItemsPerSm
+// items per SM, and when the activation rows are not 16-byte aligned (TMA bulk copies need
+// 16-byte aligned sources).
+//
+// Both kernels also read and write a bf16 state pool (ld_decode_bf16_state): the tile is the
+// same fp32 tile, widened on load and rounded to bf16 on store.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -58,6 +62,10 @@ struct Tile {
   static constexpr int kThreads = kRowGroups * kLanesPerRow;  // 256 (4 rows) or 512 (2 rows)
 };
 constexpr int kMaxTokens = LD_MAX_WIDTH;
+// One-token launches with at least this many (request, head) items per SM use the streaming
+// kernel (fp32 and bf16 pools); smaller ones and multi-token verify use one CTA per item.
+constexpr int kStreamItemsPerSm = 9;
+constexpr int kStreamItemsPerSmBf16 = 14;
 
 __device__ unsigned int g_decode_faults;
 
@@ -1644,12 +1652,13 @@ extern "C" int ld_decode(const void* qkv, int64_t qkv_row_stride, const void* a,
     if (rc != LD_OK) return rc;
   }
   if (variant == LD_DECODE_KERNEL_AUTO) {
-    // Measured on B200 (interleaved repeats on one GPU; BASELINE configs 2 and 3, 2048 x T=1,
-    // 512 x T=4, HV=48 batches 1..32): the streaming kernel is fastest for one-token decode once
-    // there are at least two (request, head) items per SM; the one-CTA-per-item kernel is fastest
-    // for multi-token verify, whose four state writes per item favour its two resident CTAs per
-    // SM, and has the lowest latency for small launches.
-    variant = (width == 1 && args.total_items >= 2 * info.sms) ? LD_DECODE_KERNEL_STREAM : LD_DECODE_KERNEL_ROWREG;
+    // Measured on B200 (CUDA-graph replay, HV=32 and 48, T=1 launches of 288..8192 items, and
+    // BASELINE configs 2 and 3): the one-CTA-per-item kernel is fastest for multi-token verify,
+    // whose four state writes per item favour its two resident CTAs per SM, and for one-token
+    // launches up to about 9 (request, head) items per SM (1,184 items: 26.5 vs 26.9 us); the
+    // streaming kernel from there on (1,472 items: 33.7 vs 36.0 us; config 2: 175 vs 188 us).
+    variant = (width == 1 && args.total_items >= kStreamItemsPerSm * info.sms) ? LD_DECODE_KERNEL_STREAM
+                                                                              : LD_DECODE_KERNEL_ROWREG;
   }
   cudaError_t err;
   if (variant != LD_DECODE_KERNEL_ROWREG) {
@@ -1732,13 +1741,15 @@ extern "C" int ld_decode_bf16_state(const void* qkv, int64_t qkv_row_stride, con
   rc = device_info(info);
   if (rc != LD_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // The streaming and one-CTA-per-item kernels have bf16-state forms; the choice follows ld_decode's.
+  // The streaming and one-CTA-per-item kernels have bf16-state forms.  With half the state bytes
+  // the one-CTA-per-item kernel stays ahead to larger one-token launches (measured on B200,
+  // HV=32: 2,048 items 35.4 vs 35.8 us, 3,072 items 60.3 vs 52.5 us, config 2 164 vs 131 us).
   const bool bulk_ok = aligned(qkv, 16) && qkv_row_stride % 8 == 0 && aligned(gate, 16) &&
                        gate_row_stride % 8 == 0 && aligned(out, 8);
   const int forced = g_kernel_override.load(std::memory_order_relaxed);
   const bool streaming = bulk_ok && (forced == LD_DECODE_KERNEL_STREAM ||
                                      (forced != LD_DECODE_KERNEL_ROWREG && width == 1 &&
-                                      args.total_items >= 2 * info.sms));
+                                      args.total_items >= kStreamItemsPerSmBf16 * info.sms));
   cudaError_t err;
   if (streaming) {
     const dim3 grid(static_cast<unsigned int>(std::min<int64_t>(args.total_items, info.sms)));

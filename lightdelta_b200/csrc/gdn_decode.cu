@@ -295,18 +295,33 @@ __device__ __forceinline__ void load_tile(const float* head, int g, int j, float
   }
 }
 
-// bf16 state pools: the same tile, four bf16 values (8 bytes) per float4, widened exactly on load
-// and rounded to nearest-even on store.
+// Column of the first of the four consecutive columns that float4 c of lane j holds.  fp32 tiles
+// use {32c + 4j}: a warp-wide 128-bit access covers whole 128-byte lines of fp32 rows.  bf16
+// pools use the wide map {64(c/2) + 8j + 4(c%2)}: each lane owns eight consecutive columns per
+// half row, so one 128-bit access moves eight bf16 values and a warp-wide access again covers
+// whole 128-byte lines.  Activations follow the map of the state they meet.
+template <bool kWide>
+__device__ __forceinline__ constexpr int tile_col(int c, int j) {
+  return kWide ? 64 * (c >> 1) + 8 * j + 4 * (c & 1) : 32 * c + 4 * j;
+}
+
+__device__ __forceinline__ float4 widen_bf16x4(uint32_t lo, uint32_t hi) {
+  return make_float4(__uint_as_float(lo << 16), __uint_as_float(lo & 0xffff0000u), __uint_as_float(hi << 16),
+                     __uint_as_float(hi & 0xffff0000u));
+}
+
+// bf16 state pools: the same fp32 tile on the wide map, eight bf16 values (16 bytes) per access,
+// widened exactly on load and rounded to nearest-even on store.
 template <int kRows>
 __device__ __forceinline__ void load_tile(const __nv_bfloat16* head, int g, int j, float4 (&s)[kRows][kVecPerRow]) {
-  const uint2* ptr = reinterpret_cast<const uint2*>(head + g * kDim + 4 * j);
+  const __nv_bfloat16* base = head + g * kDim + 8 * j;
 #pragma unroll
   for (int i = 0; i < kRows; ++i) {
 #pragma unroll
-    for (int c = 0; c < kVecPerRow; ++c) {
-      const uint2 raw = ptr[(i * Tile<kRows>::kRowGroups * kDim + c * 4 * kLanesPerRow) / 4];
-      s[i][c] = make_float4(__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xffff0000u),
-                            __uint_as_float(raw.y << 16), __uint_as_float(raw.y & 0xffff0000u));
+    for (int h = 0; h < kVecPerRow / 2; ++h) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(base + i * Tile<kRows>::kRowGroups * kDim + 64 * h);
+      s[i][2 * h] = widen_bf16x4(raw.x, raw.y);
+      s[i][2 * h + 1] = widen_bf16x4(raw.z, raw.w);
     }
   }
 }
@@ -317,26 +332,28 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 }
 
 template <int kRows, int kFirst>
-__device__ __forceinline__ void store_rows_from(uint2* ptr, const float4 (&s)[kRows][kVecPerRow]) {
+__device__ __forceinline__ void store_rows_from(__nv_bfloat16* base, const float4 (&s)[kRows][kVecPerRow]) {
 #pragma unroll
   for (int step = 0; step < kRows; ++step) {
     const int i = (step + kFirst) % kRows;
 #pragma unroll
-    for (int c = 0; c < kVecPerRow; ++c) {
-      ptr[(i * Tile<kRows>::kRowGroups * kDim + c * 4 * kLanesPerRow) / 4] =
-          make_uint2(pack_bf16x2(s[i][c].x, s[i][c].y), pack_bf16x2(s[i][c].z, s[i][c].w));
+    for (int h = 0; h < kVecPerRow / 2; ++h) {
+      const float4& a = s[i][2 * h];
+      const float4& b = s[i][2 * h + 1];
+      *reinterpret_cast<uint4*>(base + i * Tile<kRows>::kRowGroups * kDim + 64 * h) =
+          make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(b.x, b.y), pack_bf16x2(b.z, b.w));
     }
   }
 }
 
 template <int kRows>
 __device__ __forceinline__ void store_tile(__nv_bfloat16* dst_head, int g, int j, const float4 (&s)[kRows][kVecPerRow]) {
-  uint2* ptr = reinterpret_cast<uint2*>(dst_head + g * kDim + 4 * j);
+  __nv_bfloat16* base = dst_head + g * kDim + 8 * j;
   switch (blockIdx.x % kRows) {
-    case 0: store_rows_from<kRows, 0>(ptr, s); break;
-    case 1: store_rows_from<kRows, 1 % kRows>(ptr, s); break;
-    case 2: store_rows_from<kRows, 2 % kRows>(ptr, s); break;
-    default: store_rows_from<kRows, 3 % kRows>(ptr, s); break;
+    case 0: store_rows_from<kRows, 0>(base, s); break;
+    case 1: store_rows_from<kRows, 1 % kRows>(base, s); break;
+    case 2: store_rows_from<kRows, 2 % kRows>(base, s); break;
+    default: store_rows_from<kRows, 3 % kRows>(base, s); break;
   }
 }
 
@@ -467,8 +484,8 @@ __global__ void __launch_bounds__(Tile<4>::kThreads, 2) gdn_decode_rowreg_kernel
     float4 kv[kVecPerRow], qv[kVecPerRow];
 #pragma unroll
     for (int c = 0; c < kVecPerRow; ++c) {
-      kv[c] = sh_k[t][c * kLanesPerRow + j];
-      qv[c] = sh_q[t][c * kLanesPerRow + j];
+      kv[c] = sh_k[t][tile_col<sizeof(StateT) == 2>(c, j) / 4];
+      qv[c] = sh_q[t][tile_col<sizeof(StateT) == 2>(c, j) / 4];
     }
     float vrow[kRows], o[kRows];
 #pragma unroll
@@ -519,6 +536,8 @@ struct ItemInfo {
   int dst[kMaxTokens];
   float decay[kMaxTokens];
   float beta[kMaxTokens];
+  float k_inv[kMaxTokens];  // 1 / sqrt(sum k^2 + 1e-6), written by the producer once the rows land
+  float q_inv[kMaxTokens];  // the same for q, times K^-1/2
 };
 
 struct ActStage {
@@ -536,12 +555,20 @@ struct SmemT {
   using State = StateT;
   static constexpr int kStateStages = sizeof(StateT) == 4 ? kStates : 2 * kStates;
   static constexpr int kActStages = kStateStages + 1;
+  // bf16 pools: the producer reduces each token's q / k norms once and publishes them (`ready`)
+  // instead of every consumer warp reducing them.  Measured on B200, config 2: bf16 pool 129.3 ->
+  // 122.7 us; with the fp32 pool the producer's extra waits cost 175.2 -> 192.1 us, so there the
+  // consumers keep the reduction.  The producer publishes item k's norms after issuing item
+  // k + kNormLag (lag 1: 122.7 us, lag 3: 124.7 us).
+  static constexpr bool kProducerNorms = sizeof(StateT) == 2;
+  static constexpr int kNormLag = 1;
   StateT state[kStateStages][kHeadElems];
   ActStage act[kActStages];
   float out[2][kMaxTokens][kDim];
   unsigned long long full[kStateStages];
   unsigned long long empty_state[kStateStages];
   unsigned long long empty_act[kActStages];
+  unsigned long long ready[kActStages];  // the producer wrote the stage's q / k norms
   unsigned long long out_full[2];   // all consumer warps wrote their rows of out[b]
   unsigned long long out_empty[2];  // all consumer warps are past the epilogue that read out[b]
   int abort;
@@ -682,6 +709,39 @@ __device__ ItemPlan plan_item(const DecodeArgs& p, int64_t item) {
   return plan;
 }
 
+// The producer's k-th item, once its rows have landed: the q and k norms of its tokens (the
+// reduction every consumer warp would otherwise repeat), then the stage's `ready` arrival.
+// Returns false when the wait for the rows gave up.
+template <class S>
+__device__ bool publish_norms(const DecodeArgs& p, S& sm, int k, int lane) {
+  constexpr int kStates = S::kStateStages;
+  constexpr int kActs = S::kActStages;
+  const int s = k % kStates;
+  const int a = k % kActs;
+  if (!warp_wait(&sm.full[s], (k / kStates) & 1)) {
+    if (lane == 0) set_abort(sm);
+    return false;
+  }
+  ItemInfo& info = sm.act[a].info;
+  if (info.kind == kRun) {
+    for (int t = 0; t < info.n; ++t) {
+      const uint2 kr = *reinterpret_cast<const uint2*>(&sm.act[a].k[t][4 * lane]);
+      const uint2 qr = *reinterpret_cast<const uint2*>(&sm.act[a].q[t][4 * lane]);
+      const float k0 = bf16_lo(kr.x), k1 = bf16_hi(kr.x), k2 = bf16_lo(kr.y), k3 = bf16_hi(kr.y);
+      const float q0 = bf16_lo(qr.x), q1 = bf16_hi(qr.x), q2 = bf16_lo(qr.y), q3 = bf16_hi(qr.y);
+      const float k_sq = warp_sum(k0 * k0 + k1 * k1 + k2 * k2 + k3 * k3);
+      const float q_sq = warp_sum(q0 * q0 + q1 * q1 + q2 * q2 + q3 * q3);
+      if (lane == 0) {
+        info.k_inv[t] = 1.0f / sqrtf(k_sq + 1e-6f);
+        info.q_inv[t] = 1.0f / sqrtf(q_sq + 1e-6f) * p.q_scale;
+      }
+    }
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&sm.ready[a]);
+  return true;
+}
+
 // Producer warp.  Every 32 items, lane i plans the CTA's item k + i, so the dependent metadata
 // loads of 32 items share one round of memory latency; items are then issued in order from the
 // planning lane's registers: wait for a free stage, publish the plan, start the TMA bulk copies.
@@ -757,8 +817,17 @@ __device__ void produce(const DecodeArgs& p, S& sm, int lane) {
       }
     }
     __syncwarp();
+    if constexpr (S::kProducerNorms) {
+      if (k >= S::kNormLag && !publish_norms(p, sm, k - S::kNormLag, lane)) break;
+    }
   }
-  // Drain: every bulk copy this warp issued has landed before the CTA may exit.
+  // Norms of the last items, then drain: every bulk copy this warp issued has landed before the
+  // CTA may exit.
+  if constexpr (S::kProducerNorms) {
+    for (int kk = k > S::kNormLag ? k - S::kNormLag : 0; kk < k; ++kk) {
+      if (!publish_norms(p, sm, kk, lane)) break;
+    }
+  }
   if (lane == 0) {
     for (int kk = k > kStates ? k - kStates : 0; kk < k; ++kk) {
       if (!mbar_wait(&sm.full[kk % kStates], (kk / kStates) & 1)) {
@@ -769,15 +838,26 @@ __device__ void produce(const DecodeArgs& p, S& sm, int lane) {
   }
 }
 
-// Reads this lane's 16 columns {32c + 4j ..} of a bf16 head row from shared memory.
+// Reads this lane's 16 columns (tile_col<kWide>) of a bf16 head row from shared memory.
+template <bool kWide>
 __device__ __forceinline__ void load_row_cols(const __nv_bfloat16* row, int j, float4 (&v)[kVecPerRow], float& sq) {
+  if constexpr (kWide) {
+#pragma unroll
+    for (int h = 0; h < kVecPerRow / 2; ++h) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(row + 64 * h + 8 * j);
+      v[2 * h] = widen_bf16x4(raw.x, raw.y);
+      v[2 * h + 1] = widen_bf16x4(raw.z, raw.w);
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < kVecPerRow; ++c) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(row + tile_col<false>(c, j));
+      v[c] = make_float4(bf16_lo(raw.x), bf16_hi(raw.x), bf16_lo(raw.y), bf16_hi(raw.y));
+    }
+  }
   sq = 0.0f;
 #pragma unroll
-  for (int c = 0; c < kVecPerRow; ++c) {
-    const uint2 raw = *reinterpret_cast<const uint2*>(row + c * 4 * kLanesPerRow + 4 * j);
-    v[c] = make_float4(bf16_lo(raw.x), bf16_hi(raw.x), bf16_lo(raw.y), bf16_hi(raw.y));
-    sq += v[c].x * v[c].x + v[c].y * v[c].y + v[c].z * v[c].z + v[c].w * v[c].w;
-  }
+  for (int c = 0; c < kVecPerRow; ++c) sq += v[c].x * v[c].x + v[c].y * v[c].y + v[c].z * v[c].z + v[c].w * v[c].w;
 }
 
 template <int kRows, class S>
@@ -802,6 +882,10 @@ __device__ void consume(const DecodeArgs& p, S& sm, int tid) {
     const int s = k % kStates;
     const int a = k % kActs;
     if (!warp_wait(&sm.full[s], (k / kStates) & 1)) {
+      if (lane == 0) set_abort(sm);
+      break;
+    }
+    if (S::kProducerNorms && !warp_wait(&sm.ready[a], (k / kActs) & 1)) {
       if (lane == 0) set_abort(sm);
       break;
     }
@@ -844,18 +928,29 @@ __device__ void consume(const DecodeArgs& p, S& sm, int tid) {
     for (int t = 0; t < n; ++t) {
       float4 kv[kVecPerRow], qv[kVecPerRow];
       float k_sq, q_sq;
-      load_row_cols(act.k[t], j, kv, k_sq);
-      load_row_cols(act.q[t], j, qv, q_sq);
-      k_sq = row_sum(k_sq);
-      q_sq = row_sum(q_sq);
-      // L2 norm in fp32 as gdn.py:98-99; q then scaled by K^-1/2 as gdn.py:101.
-      const float k_inv = 1.0f / sqrtf(k_sq + 1e-6f);
-      const float q_inv = 1.0f / sqrtf(q_sq + 1e-6f);
+      load_row_cols<sizeof(State) == 2>(act.k[t], j, kv, k_sq);
+      load_row_cols<sizeof(State) == 2>(act.q[t], j, qv, q_sq);
+      // L2 norms in fp32 as gdn.py:98-99; q then scaled by K^-1/2 as gdn.py:101.  With a bf16
+      // pool the producer has reduced them already.
+      if constexpr (S::kProducerNorms) {
+        const float k_inv = info.k_inv[t];
+        const float q_inv = info.q_inv[t];
 #pragma unroll
-      for (int c = 0; c < kVecPerRow; ++c) {
-        kv[c] = make_float4(kv[c].x * k_inv, kv[c].y * k_inv, kv[c].z * k_inv, kv[c].w * k_inv);
-        qv[c] = make_float4(qv[c].x * q_inv * p.q_scale, qv[c].y * q_inv * p.q_scale, qv[c].z * q_inv * p.q_scale,
-                            qv[c].w * q_inv * p.q_scale);
+        for (int c = 0; c < kVecPerRow; ++c) {
+          kv[c] = make_float4(kv[c].x * k_inv, kv[c].y * k_inv, kv[c].z * k_inv, kv[c].w * k_inv);
+          qv[c] = make_float4(qv[c].x * q_inv, qv[c].y * q_inv, qv[c].z * q_inv, qv[c].w * q_inv);
+        }
+      } else {
+        k_sq = row_sum(k_sq);
+        q_sq = row_sum(q_sq);
+        const float k_inv = 1.0f / sqrtf(k_sq + 1e-6f);
+        const float q_inv = 1.0f / sqrtf(q_sq + 1e-6f);
+#pragma unroll
+        for (int c = 0; c < kVecPerRow; ++c) {
+          kv[c] = make_float4(kv[c].x * k_inv, kv[c].y * k_inv, kv[c].z * k_inv, kv[c].w * k_inv);
+          qv[c] = make_float4(qv[c].x * q_inv * p.q_scale, qv[c].y * q_inv * p.q_scale,
+                              qv[c].z * q_inv * p.q_scale, qv[c].w * q_inv * p.q_scale);
+        }
       }
       float vrow[kRows], o[kRows];
 #pragma unroll
@@ -925,7 +1020,10 @@ __global__ void __maxnreg__(168) gdn_decode_stream_kernel(const DecodeArgs p) {
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty_state[s], kConsumerWarps);
     }
-    for (int a = 0; a < kActs; ++a) mbar_init(&sm.empty_act[a], kConsumerWarps);
+    for (int a = 0; a < kActs; ++a) {
+      mbar_init(&sm.empty_act[a], kConsumerWarps);
+      mbar_init(&sm.ready[a], 1);
+    }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sm.out_full[b], kConsumerWarps);
       mbar_init(&sm.out_empty[b], kConsumerWarps);
@@ -963,6 +1061,7 @@ constexpr int kThreads = kConsumers + 64;        // + producer warp + storer war
 template <int kLoads, int kStaging>
 struct Smem {
   using State = float;
+  static constexpr bool kProducerNorms = false;
   static constexpr int kStateStages = kLoads;
   static constexpr int kActStages = kLoads + 1;
   float state[kLoads][kHeadElems];
@@ -1041,8 +1140,8 @@ __device__ void consume(const DecodeArgs& p, Smem<kLoads, kStaging>& sm, int tid
     for (int t = 0; t < n; ++t) {
       float4 kv[kVecPerRow], qv[kVecPerRow];
       float k_sq, q_sq;
-      load_row_cols(act.k[t], j, kv, k_sq);
-      load_row_cols(act.q[t], j, qv, q_sq);
+      load_row_cols<false>(act.k[t], j, kv, k_sq);
+      load_row_cols<false>(act.q[t], j, qv, q_sq);
       k_sq = row_sum(k_sq);
       q_sq = row_sum(q_sq);
       // L2 norm in fp32 as gdn.py:98-99; q then scaled by K^-1/2 as gdn.py:101.
@@ -1369,8 +1468,8 @@ __device__ __forceinline__ void staged_body(const DecodeArgs& p, Smem<Q>& sm) {
     for (int t = 0; t < n; ++t) {
       float4 kv[kVecPerRow], qv[kVecPerRow];
       float k_sq, q_sq;
-      load_row_cols(sm.k[t], j, kv, k_sq);
-      load_row_cols(sm.q[t], j, qv, q_sq);
+      load_row_cols<false>(sm.k[t], j, kv, k_sq);
+      load_row_cols<false>(sm.q[t], j, qv, q_sq);
       k_sq = row_sum(k_sq);
       q_sq = row_sum(q_sq);
       // L2 norm in fp32 as gdn.py:98-99; q then scaled by K^-1/2 as gdn.py:101.

@@ -1,11 +1,12 @@
 """GPU parity of torch.ops.lightdelta.decode_bf16_state / ld_decode_bf16_state (decode and MTP
 verify on a bf16 state pool).
 
-Two expectations: (1) bit-exact against the fp32 decode kernel run on the same pool widened to
-fp32 (identical outputs, stored states equal to its fp32 states rounded to bf16); (2) the
-oracle's bf16-pool mode (fp32 recurrence, each stored step rounded), outputs within the
-reference test's tolerance with at most 1e-3 outside 2e-3, stored states within one bf16 ulp or
-the fp32 state tolerance."""
+Two expectations: (1) the oracle's bf16-pool mode (fp32 recurrence, each stored step rounded):
+outputs within the reference test's tolerance with at most 1e-3 outside 2e-3, stored states within
+one bf16 ulp or the fp32 state tolerance; (2) the fp32 decode kernel run on the same pool widened
+to fp32, to the same tolerances against its states rounded to bf16.  The bf16 tiles assign
+columns to lanes differently from the fp32 tiles (eight consecutive bf16 columns per lane), so
+the two kernels' dot products add in different orders and agree to rounding, not bit for bit."""
 
 import dataclasses
 
@@ -97,23 +98,27 @@ def test_head_geometries(device, heads):
 
 
 @pytest.mark.parametrize("shape", [(256, 1, "ones"), (64, 4, "uniform"), (5, 3, "uniform")])
-def test_bit_exact_against_the_fp32_kernel_on_the_widened_pool(device, kernel, shape):
-    """The bf16 pool changes only the state's load and store: outputs are identical to the fp32
-    decode on the widened pool and every stored state is that kernel's fp32 state rounded."""
+def test_matches_the_fp32_kernel_on_the_widened_pool(device, kernel, shape):
+    """The bf16 pool changes the state's load and store: outputs match the fp32 decode on the
+    widened pool and every stored state is that kernel's fp32 state rounded, to rounding."""
     batch, width, accepted = shape
     case = bf16_case(batch, width, 1 + batch * width + 7, device=device, seed=80 + width, accepted=accepted)
     fp32 = dataclasses.replace(case, pool=case.pool.float(), out=torch.empty_like(case.out))
     run(case)
     torch.ops.lightdelta.decode(*fp32.op_args())
     torch.cuda.synchronize()
-    assert torch.equal(case.out, fp32.out)
-    assert torch.equal(case.pool, fp32.pool.to(torch.bfloat16))
+    assert_out_close_tail(bits(case.out), bits(fp32.out), "out vs fp32 kernel")
+    assert_bf16_state_close(bits(case.pool), bits(fp32.pool.to(torch.bfloat16)), "pool vs fp32 kernel")
+    untouched = torch.ones(case.pool.shape[0], dtype=torch.bool, device=device)
+    untouched[case.slots.flatten().long()] = False
+    assert torch.equal(case.pool[untouched], fp32.pool[untouched].to(torch.bfloat16))
 
 
-def test_chained_launches_equal_the_fp32_kernel_rounded_between_steps(device, kernel):
+def test_chained_launches_track_the_fp32_kernel_rounded_between_steps(device, kernel):
     """Three in-place launches back to back (each reads what the previous one stored; with
     programmatic dependent launch they overlap their prologues) against the fp32 kernel whose
-    pool is rounded to bf16 after every launch: identical outputs and pools at every step."""
+    pool is rounded to bf16 after every launch: outputs at every step and the final pool agree to
+    rounding (k ulps after k launches)."""
     case = bf16_case(16, 1, 40, device=device, seed=12)
     fp32 = dataclasses.replace(case, pool=case.pool.float(), out=torch.empty_like(case.out))
     outs = []
@@ -124,8 +129,8 @@ def test_chained_launches_equal_the_fp32_kernel_rounded_between_steps(device, ke
         torch.ops.lightdelta.decode(*fp32.op_args())
         fp32.pool.copy_(fp32.pool.to(torch.bfloat16).float())
         torch.cuda.synchronize()
-        assert torch.equal(outs[step], fp32.out), f"step {step + 1}"
-    assert torch.equal(case.pool, fp32.pool.to(torch.bfloat16))
+        assert_out_close_tail(bits(outs[step]), bits(fp32.out), f"step {step + 1} out")
+    assert_bf16_state_close(bits(case.pool), bits(fp32.pool.to(torch.bfloat16)), "pool after 3 steps", max_ulps=3)
 
 
 def test_invalid_requests_and_fault_word(device, kernel):

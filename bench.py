@@ -693,8 +693,12 @@ def run_reference(args, dist: Dist) -> dict | None:
     import oracle
     from lightdelta_b200 import workloads
 
-    if args.workload == "copy":
-        return {"impl": "reference", "unavailable": "the copy workload has no CPU arm in this harness"}
+    if args.workload in ("decode_bf16", "verify_bf16"):
+        return {"impl": "reference",
+                "unavailable": "the reference supports only an fp32 state pool (csrc/gdn_decode.cu:375-377)"}
+    if args.workload not in ("decode", "verify"):
+        return {"impl": "reference", "unavailable": f"the {args.workload} workload has no reference CPU arm in this "
+                                                    "harness (the decode and verify workloads do)"}
     device = torch.device("cuda", dist.local_rank) if torch.cuda.is_available() else torch.device("cpu")
     case = workloads.config2(device, seed=2) if args.workload == "decode" else workloads.config3(device, seed=3)
     threads = oracle.default_threads()

@@ -42,3 +42,13 @@ def test_reference_arm_prints_one_contract_line():
     assert line["e2e"] == {"value": line["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
     assert line["config"]["workload"] == "config2_decode"
+
+
+@pytest.mark.parametrize("workload", ["decode_bf16", "commit"])
+def test_reference_arm_without_a_cpu_path_says_so(workload):
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    result = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--workload", workload,
+                             "--steps", "3", "--warmup", "3"], capture_output=True, text=True, timeout=600, env=env,
+                            check=True)
+    line = json.loads(result.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and "unavailable" in line

@@ -21,7 +21,9 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 OUT_DIR = HERE / "_ref"
 OUT = OUT_DIR / "_C.so"
-DEFAULT_REFERENCE = Path("/root/reference")
+# The reference checkout sits beside this repository ("reference" next to the repo's directory);
+# LIGHTDELTA_REFERENCE overrides it.
+DEFAULT_REFERENCE = Path(os.environ.get("LIGHTDELTA_REFERENCE", HERE.parent.parent / "reference"))
 SOURCES = ("csrc/register.cpp", "csrc/gdn_decode.cu", "csrc/state_io.cu")
 
 

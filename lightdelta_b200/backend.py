@@ -14,6 +14,9 @@ has the reference's call signature and state semantics:
 
 Only ``compute = "cuda_fused"`` exists here: the reference's Torch compute mode is this
 project's parity oracle and is not offered as a product path.
+
+A bf16 pool (an extension; the reference's pool is fp32) runs in indexed mode through
+``lightdelta::decode_bf16_state``.  Packed mode keeps the reference's fp32-only state copies.
 """
 
 from __future__ import annotations
@@ -42,8 +45,12 @@ class GDNBackend:
         batch, width = slots.shape
         self.calls["decode" if width == 1 else "verify"] += 1
         if self.config.state_io == "indexed":
-            torch.ops.lightdelta.decode(qkv, a, b, a_log, dt_bias, slots, cu, accepted, pool, gate, weight, out, eps)
+            op = torch.ops.lightdelta.decode_bf16_state if pool.dtype == torch.bfloat16 else torch.ops.lightdelta.decode
+            op(qkv, a, b, a_log, dt_bias, slots, cu, accepted, pool, gate, weight, out, eps)
             return
+        if pool.dtype != torch.float32:
+            raise ValueError("packed state I/O needs an fp32 pool (gather_state and scatter_state copy fp32 slots); "
+                             "use state_io='indexed' for a bf16 pool")
 
         key = (pool.device, batch, width, tuple(pool.shape[1:]))
         if key not in self._packed:

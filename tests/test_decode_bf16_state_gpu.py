@@ -175,3 +175,19 @@ def test_rejects_an_fp32_pool_and_a_misaligned_stride(device):
     case.pool = pool
     with pytest.raises(RuntimeError, match="slot stride"):
         torch.ops.lightdelta.decode_bf16_state(*case.op_args())
+
+
+def test_indexed_backend_runs_a_bf16_pool(device):
+    from lightdelta_b200.backend import GDNBackend
+    from lightdelta_b200.config import BackendConfig
+
+    case = bf16_case(4, 2, 16, device=device, seed=21, accepted="uniform")
+    direct = dataclasses.replace(case, pool=case.pool.clone(), out=torch.empty_like(case.out))
+    backend = GDNBackend(BackendConfig(compute="cuda_fused", state_io="indexed"))
+    backend(*case.op_args())
+    torch.ops.lightdelta.decode_bf16_state(*direct.op_args())
+    torch.cuda.synchronize()
+    assert torch.equal(case.out, direct.out) and torch.equal(case.pool, direct.pool)
+    packed = GDNBackend(BackendConfig(compute="cuda_fused", state_io="packed"))
+    with pytest.raises(ValueError, match="fp32 pool"):
+        packed(*case.op_args())

@@ -30,8 +30,10 @@
 // items per SM, and when the activation rows are not 16-byte aligned (TMA bulk copies need
 // 16-byte aligned sources).
 //
-// Both kernels also read and write a bf16 state pool (ld_decode_bf16_state): the tile is the
-// same fp32 tile, widened on load and rounded to bf16 on store.
+// Both kernels also read and write a bf16 state pool (ld_decode_bf16_state): the tile is an fp32
+// tile, widened on load and rounded to bf16 on store, with each lane owning eight consecutive
+// columns per half row ({64h + 8j .. 64h + 8j + 7 : h = 0, 1}, see tile_col) so that its state
+// accesses stay 16 bytes wide.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 

@@ -1,6 +1,7 @@
 """CPU tests of the conv1d state-update oracle (oracle/conv_oracle.c) against golden fixtures
 made by vLLM's own causal_conv1d_update kernel (tests/golden/make_golden_conv.py), the
-algorithm the reference calls at python/lightdelta/integration/vllm_layer.py:161-172, :199-207."""
+algorithm the reference calls at python/lightdelta/integration/vllm_layer.py:161-172, :199-207;
+and the host-side argument checks of ld_conv_update (nothing is launched)."""
 
 import numpy as np
 import pytest
@@ -44,3 +45,27 @@ def test_bf16_products_are_rounded():
         acc = acc + p
     expected = detrand.bf16_bits(acc / (np.float32(1) + np.exp(-acc)))
     assert np.abs(y[0].astype(np.int32) - expected.astype(np.int32)).max() <= 1
+
+
+@pytest.mark.parametrize("change, message", [
+    ({12: 7}, "kernel width"),           # conv_width
+    ({18: 5}, "tokens per request"),     # max_tokens
+    ({9: 2, 18: 2}, "state length"),     # conv_state_len < width - 2 + max_tokens
+    ({3: 0}, "dim >= 1"),                # dim
+    ({1: 10}, "invalid strides"),        # x_row_stride < dim
+    ({0: None}, "NULL"),                 # x
+    ({0: 1 << 20 | 1}, "2-byte aligned"),
+])
+def test_capi_conv_update_rejects_bad_arguments_before_touching_the_gpu(native, change, message):
+    """Host-side checks only: the addresses are never dereferenced (each call fails validation)."""
+    fake = 1 << 20
+    args = [fake, 64, 4, 64, fake, 8, 192, 3, 1, 3, fake, None, 4, fake, 1, None, fake, 4, 1, None]
+    for index, value in change.items():
+        args[index] = value
+    assert native.lib().ld_conv_update(*args) == native.LD_ERR_INVALID
+    assert message in native.last_error()
+
+
+def test_capi_conv_update_without_requests_is_a_no_op(native):
+    args = [None, 64, 0, 64, None, 8, 192, 3, 1, 3, None, None, 4, None, 1, None, None, 0, 1, None]
+    assert native.lib().ld_conv_update(*args) == native.LD_OK

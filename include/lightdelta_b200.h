@@ -163,7 +163,8 @@ int ld_copy_slots(float* pool, int64_t n_pool_slots, int64_t pool_slot_stride,
  * multiple of 8): each request's source state is widened to fp32, updated in fp32 across its
  * tokens exactly as ld_decode does, and every stored step is rounded to bf16 (nearest even).
  * Half the state bytes of an fp32 pool per token; results differ from the fp32 pool by that
- * rounding.  The streaming and one-CTA-per-item kernels run it (ld_decode_kernel_override's
+ * rounding and, within fp32 rounding, by the order of the dot products' additions (each lane
+ * owns eight consecutive bf16 columns).  The streaming and one-CTA-per-item kernels run it (ld_decode_kernel_override's
  * other variants fall back to the automatic choice).  No counterpart in the reference, whose
  * launcher requires an fp32 pool (csrc/gdn_decode.cu:375-377).
  */

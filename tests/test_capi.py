@@ -123,3 +123,17 @@ def test_cpu_tensors_have_no_kernel(native):
     pool = torch.zeros(2, 1, 4, 4)
     with pytest.raises((RuntimeError, NotImplementedError)):
         torch.ops.lightdelta.scatter_state(torch.zeros(1, 1, 4, 4), torch.ones(1, dtype=torch.int32), pool)
+
+
+def test_process_wide_toggles(native):
+    """Kernel override and programmatic-launch switches: set, query and restore (no launch)."""
+    lib = native.lib()
+    previous = lib.ld_decode_kernel_override(native.DECODE_KERNELS["rowreg"])
+    assert lib.ld_decode_kernel_override(previous) == native.DECODE_KERNELS["rowreg"]
+    assert lib.ld_decode_kernel_override(99) == -native.LD_ERR_INVALID
+    enabled = lib.ld_programmatic_launch(-1)
+    assert enabled in (0, 1)
+    assert lib.ld_programmatic_launch(0) == enabled
+    assert lib.ld_programmatic_launch(-1) == 0
+    assert lib.ld_programmatic_launch(enabled) == 0
+    assert lib.ld_programmatic_launch(-1) == enabled

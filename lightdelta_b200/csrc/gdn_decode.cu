@@ -525,7 +525,6 @@ __global__ void __launch_bounds__(Tile<4>::kThreads, 2) gdn_decode_rowreg_kernel
 namespace stream {
 
 constexpr int kStates = 3;                            // fp32 state ring depth (64 KiB each)
-constexpr int kActs = kStates + 1;                    // activation ring depth
 constexpr uint64_t kWaitLimitNs = 1000000000ull;      // 1 s bound on every mbarrier wait
 
 enum ItemKind : int { kSkip = 0, kZero = 1, kRun = 2 };

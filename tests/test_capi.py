@@ -1,6 +1,7 @@
 """CPU tests of the drop-in boundary: the C-ABI library loads and exports every declared
-symbol, host-side argument validation, and the torch.library schemas match the reference's
-(csrc/register.cpp:4-11).  Nothing here launches a kernel."""
+symbol, host-side argument validation, the torch.library schemas match the reference's
+(csrc/register.cpp:4-11), and the build loads through the reference's own loader route as
+`lightdelta._C`.  Nothing here launches a kernel."""
 
 import ctypes
 import re
@@ -137,3 +138,28 @@ def test_process_wide_toggles(native):
     assert lib.ld_programmatic_launch(-1) == 0
     assert lib.ld_programmatic_launch(enabled) == 0
     assert lib.ld_programmatic_launch(-1) == enabled
+
+
+def test_loads_as_the_reference_package_extension(native, tmp_path):
+    """The drop-in route of the reference's loader (python/lightdelta/ops/__init__.py:7 finds
+    `lightdelta._C` with importlib and loads it with torch.ops.load_library): with the two
+    libraries installed as that package's `_C.so`, the reference's three schemas register."""
+    import json
+    import shutil
+    import subprocess
+    import sys
+
+    package = tmp_path / "lightdelta"
+    package.mkdir()
+    (package / "__init__.py").write_text("")
+    shutil.copy(native.LIB_PATH.parent / "_C.so", package / "_C.so")
+    shutil.copy(native.LIB_PATH, package / native.LIB_PATH.name)
+    script = (
+        "import importlib.util, json, torch\n"
+        "torch.ops.load_library(importlib.util.find_spec('lightdelta._C').origin)\n"
+        "print(json.dumps({n: str(getattr(torch.ops.lightdelta, n).default._schema)"
+        " for n in ('decode', 'gather_state', 'scatter_state')}))\n"
+    )
+    result = subprocess.run([sys.executable, "-c", script], cwd=tmp_path, capture_output=True, text=True,
+                            timeout=300, check=True)
+    assert json.loads(result.stdout.strip().splitlines()[-1]) == REFERENCE_SCHEMAS

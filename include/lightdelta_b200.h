@@ -288,6 +288,41 @@ int ld_greedy_verify(const void* logits, int logits_dtype, int64_t n_logits, int
  */
 int ld_greedy_verify_cluster_override(int cluster);
 
+/* Size of the static device scratch of ld_decode_packed_noalloc (64 MiB on every GPU that loads
+ * the library, held until the process exits): 32 KiB of per-call request plan, then the fp32
+ * scratch state slots. */
+#define LD_NOALLOC_SCRATCH_BYTES (64LL * 1024 * 1024)
+
+/*
+ * Packed-mode decode / MTP verify that allocates nothing.  It has no counterpart in the
+ * reference; it exists for callers that cannot allocate device memory while they decode: a host
+ * that binds this C ABI from a runtime with no device allocator of its own, an engine that hands
+ * the whole GPU to its state pools at start-up and forbids later allocations, or a latency-bound
+ * loop that cannot afford cudaMalloc's implicit device-wide synchronisation.
+ *
+ * Arguments, results and errors are those of ld_decode (state = the fp32 pool).  It computes what
+ * the packed state path computes (python/lightdelta/backend.py:30-91): each request's source state
+ * is gathered into a scratch slot, decoded there, and every live step state is committed to its
+ * pool slot (null destinations skipped).  Outputs and pool contents equal ld_decode's.
+ * The scratch is one static device array of LD_NOALLOC_SCRATCH_BYTES:
+ *   - it must hold (1 + n_requests * width) slots of num_v_heads * 64 KiB after its 32 KiB plan
+ *     region (at num_v_heads = 32: n_requests * width <= 30), and n_requests * width <= 1024;
+ *     larger calls return LD_ERR_INVALID with a message, before any launch;
+ *   - the first call on each device looks up the array's device address (cudaGetSymbolAddress
+ *     with that device current) and keeps it; make that first call before any stream capture;
+ *   - every call overwrites the parts it reads, so nothing needs clearing between calls, but all
+ *     calls on a device share the array: calls whose work overlaps on the GPU (other streams,
+ *     other host threads) race and corrupt each other's results.
+ * No cudaMalloc, cudaFree or other allocating routine is called.
+ */
+int ld_decode_packed_noalloc(const void* qkv, int64_t qkv_row_stride, const void* a, int64_t a_row_stride,
+                             const void* b, int64_t b_row_stride, const float* a_log, const void* dt_bias,
+                             int dt_bias_dtype, const int32_t* indices, int64_t n_requests, int64_t width,
+                             const int32_t* cu, const int32_t* accepted, float* state, int64_t n_slots,
+                             int64_t slot_stride, const void* gate, int64_t gate_row_stride, const void* weight,
+                             int weight_dtype, void* out, int64_t n_tokens, int64_t num_k_heads,
+                             int64_t num_v_heads, float eps, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

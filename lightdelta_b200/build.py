@@ -32,7 +32,7 @@ TORCH_LIB = PKG / "_C.so"
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall"]
 
-CAPI_SOURCES = ["gdn_decode.cu", "state_io.cu", "greedy_verify.cu", "conv_update.cu", "capi.cpp"]
+CAPI_SOURCES = ["gdn_decode.cu", "state_io.cu", "greedy_verify.cu", "conv_update.cu", "decode_noalloc.cu", "capi.cpp"]
 CAPI_HEADERS = ["internal.h", "exports.map"]
 
 

@@ -245,3 +245,24 @@ def conv_update(x, conv_state, conv_weight, conv_bias, slots, accepted, cu, max_
         None if accepted is None else accepted.data_ptr(), cu.data_ptr(), slots.numel(), int(max_tokens),
         _stream(x, stream),
     ))
+
+
+def decode_packed_noalloc(qkv, a, b, a_log, dt_bias, indices, cu, accepted, state, gate, weight, out, eps=1e-6,
+                          stream=None):
+    """ld_decode_packed_noalloc on torch tensors laid out as torch.ops.lightdelta.decode expects:
+    the packed state path with its scratch in the library's static device array (fp32 pool only;
+    at most LD_NOALLOC_SCRATCH_BYTES of scratch, see include/lightdelta_b200.h)."""
+    handle = lib()
+    entry = handle.ld_decode_packed_noalloc
+    if entry.argtypes is None:
+        entry.argtypes = handle.ld_decode.argtypes
+        entry.restype = ctypes.c_int
+    hv = state.shape[1]
+    h = (qkv.shape[1] // HEAD_DIM - hv) // 2
+    check(entry(
+        qkv.data_ptr(), qkv.stride(0), a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), a_log.data_ptr(),
+        dt_bias.data_ptr(), _dtype_code(dt_bias), indices.data_ptr(), indices.shape[0], indices.shape[1],
+        cu.data_ptr(), accepted.data_ptr(), state.data_ptr(), state.shape[0], state.stride(0), gate.data_ptr(),
+        gate.stride(0), weight.data_ptr(), _dtype_code(weight), out.data_ptr(), qkv.shape[0], h, hv, float(eps),
+        _stream(qkv, stream),
+    ))

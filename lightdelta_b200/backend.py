@@ -13,7 +13,9 @@ has the reference's call signature and state semantics:
   pool[0] onto itself does).
 
 Only ``compute = "cuda_fused"`` exists here: the reference's Torch compute mode is this
-project's parity oracle and is not offered as a product path.
+project's parity oracle and is not offered as a product path.  The config may be this package's
+``BackendConfig`` or the reference's own (``python/lightdelta/config.py``): the backend calls its
+``validate()`` and reads only ``compute`` and ``state_io``.
 
 A bf16 pool (an extension; the reference's pool is fp32) runs in indexed mode through
 ``lightdelta::decode_bf16_state``.  Packed mode keeps the reference's fp32-only state copies.
@@ -26,17 +28,18 @@ from collections import Counter
 import torch
 
 from lightdelta_b200 import ops  # noqa: F401 -- registers torch.ops.lightdelta
-from lightdelta_b200.config import BackendConfig
 
 
 class GDNBackend:
-    def __init__(self, config: BackendConfig):
+    def __init__(self, config):
         config.validate()
-        if config.compute != "cuda_fused":
+        if getattr(config, "compute", None) != "cuda_fused":
             raise ValueError(
                 "lightdelta_b200 implements compute='cuda_fused' only; the Torch reference compute "
                 "mode is the parity oracle, not a backend"
             )
+        if getattr(config, "state_io", None) not in ("packed", "indexed"):
+            raise ValueError("state_io must be packed or indexed")
         self.config = config
         self.calls = Counter()
         self._packed: dict = {}

@@ -69,3 +69,50 @@ def test_packed_mode_refuses_a_bf16_pool_before_launching(native):
     pool = torch.zeros(3, 2, 128, 128, dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="fp32 pool"):
         backend(None, None, None, None, None, slots, None, None, pool, None, None, None)
+
+
+def test_the_reference_config_files_load_unchanged():
+    """Every configs/*.toml of the reference checkout (when it sits beside this repository) loads,
+    and each field agrees with a plain TOML read of the file."""
+    import tomllib
+    from pathlib import Path
+
+    configs = Path(__file__).resolve().parent.parent.parent / "reference" / "configs"
+    files = sorted(configs.glob("*.toml")) if configs.is_dir() else []
+    if not files:
+        pytest.skip("reference checkout not present")
+    for path in files:
+        config = BackendConfig.from_file(path)
+        raw = tomllib.loads(path.read_text())
+        for section, attr_of in (("gdn", {}), ("runtime", {}),
+                                 ("speculation", {"method": "speculation_method"})):
+            for key, value in raw.get(section, {}).items():
+                assert getattr(config, attr_of.get(key, key)) == value, (path.name, key)
+
+
+def test_schema_covers_every_field_and_default():
+    from lightdelta_b200 import config as cfg
+
+    assert [o.attr for o in cfg.SCHEMA] == list(BackendConfig.__dataclass_fields__)
+    defaults = BackendConfig()
+    assert all(getattr(defaults, o.attr) == o.default for o in cfg.SCHEMA)
+
+
+def test_bool_is_not_accepted_for_an_int_field():
+    with pytest.raises(ValueError, match="Invalid type for num_speculative_tokens"):
+        BackendConfig(speculation_method="mtp", num_speculative_tokens=True).validate()
+
+
+def test_backend_accepts_the_callers_own_config_object(native):
+    """The reference's callers build its own BackendConfig; GDNBackend reads compute and
+    state_io from any such object after calling its validate()."""
+    from types import SimpleNamespace
+
+    from lightdelta_b200.backend import GDNBackend
+
+    calls = []
+    foreign = SimpleNamespace(compute="cuda_fused", state_io="indexed", validate=lambda: calls.append(1))
+    backend = GDNBackend(foreign)
+    assert backend.config is foreign and calls == [1]
+    with pytest.raises(ValueError, match="state_io must be"):
+        GDNBackend(SimpleNamespace(compute="cuda_fused", state_io="paged", validate=lambda: None))

@@ -45,7 +45,7 @@ extern "C" {
 #define LD_FAULT_GATHER_SLOT_RANGE 0x4u   /* gather_state: a slot index >= n_pool_slots */
 #define LD_FAULT_SCATTER_SLOT_RANGE 0x8u  /* scatter_state: a slot index >= n_pool_slots */
 #define LD_FAULT_COPY_SLOT_RANGE 0x10u    /* copy_slots: a slot index >= n_pool_slots */
-#define LD_FAULT_WAIT_TIMEOUT 0x20u       /* a bounded in-kernel wait expired; that launch's results are incomplete */
+#define LD_FAULT_WAIT_TIMEOUT 0x20u       /* a bounded in-kernel wait expired: the CTA stored nothing more and returned */
 #define LD_FAULT_VERIFY_DRAFTS 0x40u      /* greedy_verify: a request has more drafts than steps */
 #define LD_FAULT_VERIFY_RANGE 0x80u       /* greedy_verify: metadata points outside the logits or token ids */
 #define LD_FAULT_CONV_SLOT_RANGE 0x100u   /* conv update: a conv-state slot index >= n_conv_slots */
@@ -153,10 +153,6 @@ int ld_copy_slots(float* pool, int64_t n_pool_slots, int64_t pool_slot_stride,
 #define LD_DECODE_KERNEL_AUTO 0        /* library default: STREAM for width-1 launches of >= 9 items per SM (>= 14 with a bf16 pool), else ROWREG */
 #define LD_DECODE_KERNEL_ROWREG 1      /* one CTA per (request, head), state loaded into registers */
 #define LD_DECODE_KERNEL_STREAM 2      /* persistent kernel: TMA bulk loads into a 3-deep ring, 8 consumer warps */
-#define LD_DECODE_KERNEL_TMA_STORE 3   /* persistent kernel with TMA bulk loads and TMA bulk stores */
-#define LD_DECODE_KERNEL_STAGED_Q1 4   /* one CTA per (request, head), TMA-staged state, 3 CTAs/SM */
-#define LD_DECODE_KERNEL_STAGED_Q2 5   /* two-CTA cluster per (request, head), 64 rows each */
-#define LD_DECODE_KERNEL_STAGED_Q4 6   /* four-CTA cluster per (request, head), 32 rows each */
 
 /*
  * ld_decode on a bf16 state pool (state: bf16 [n_slots, HV, 128, 128], slot_stride elements, a
@@ -164,8 +160,8 @@ int ld_copy_slots(float* pool, int64_t n_pool_slots, int64_t pool_slot_stride,
  * tokens exactly as ld_decode does, and every stored step is rounded to bf16 (nearest even).
  * Half the state bytes of an fp32 pool per token; results differ from the fp32 pool by that
  * rounding and, within fp32 rounding, by the order of the dot products' additions (each lane
- * owns eight consecutive bf16 columns).  The streaming and one-CTA-per-item kernels run it (ld_decode_kernel_override's
- * other variants fall back to the automatic choice).  No counterpart in the reference, whose
+ * owns eight consecutive bf16 columns).  The streaming and one-CTA-per-item kernels both run it
+ * (ld_decode_kernel_override applies).  No counterpart in the reference, whose
  * launcher requires an fp32 pool (csrc/gdn_decode.cu:375-377).
  */
 int ld_decode_bf16_state(const void* qkv, int64_t qkv_row_stride, const void* a, int64_t a_row_stride,
@@ -224,12 +220,24 @@ int ld_conv_decode(void* qkv, int64_t qkv_row_stride, const void* a, int64_t a_r
 
 /*
  * Process-wide choice of the kernel that ld_decode launches, for tuning and for testing every
- * variant against the oracle; all variants compute the same results.  Streaming variants need
- * 16-byte aligned qkv / gate rows and fall back to LD_DECODE_KERNEL_ROWREG otherwise.
+ * variant against the oracle; all variants compute the same results.  The streaming kernel needs
+ * 16-byte aligned qkv / gate rows and falls back to LD_DECODE_KERNEL_ROWREG otherwise.
  * Returns the previous setting, or -LD_ERR_INVALID for an unknown variant.
  * No counterpart in the reference, which has a single kernel (csrc/gdn_decode.cu:130).
  */
 int ld_decode_kernel_override(int variant);
+
+/*
+ * Test hook of the persistent decode kernel's bounded waits, process-wide; no counterpart in the
+ * reference.  Every mbarrier wait of that kernel gives up after limit_ns nanoseconds (0 restores
+ * the default of one second), raises LD_FAULT_WAIT_TIMEOUT, and the CTA stops: it stores no state
+ * or output of the item whose wait ran out or of any later item, waits (bounded) for the copies it
+ * issued and returns.  extra_tx_bytes > 0 (at most 1024) makes every state load announce that many
+ * bytes more than it copies, so the waits for it run out although every copy lands: a launch then
+ * changes no pool slot and no output of a request it runs.  Settings apply to launches made after
+ * the call.  Returns LD_OK, or LD_ERR_INVALID for arguments out of range.
+ */
+int ld_decode_wait_test(int64_t limit_ns, int32_t extra_tx_bytes);
 
 /*
  * Programmatic dependent launch (PDL), process-wide: 1 (the default) launches every kernel

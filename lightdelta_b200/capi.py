@@ -33,7 +33,7 @@ LD_FAULT_CONV_SLOT_RANGE = 0x100
 HEAD_DIM = 128
 MAX_WIDTH = 4
 MAX_VERIFY_STEPS = 7
-DECODE_KERNELS = {"auto": 0, "rowreg": 1, "stream": 2, "tmastore": 3, "staged1": 4, "staged2": 5, "staged4": 6}
+DECODE_KERNELS = {"auto": 0, "rowreg": 1, "stream": 2}
 
 _lib: ctypes.CDLL | None = None
 
@@ -88,6 +88,8 @@ def lib() -> ctypes.CDLL:
     handle.ld_conv_update.restype = i32
     handle.ld_programmatic_launch.argtypes = [i32]
     handle.ld_programmatic_launch.restype = i32
+    handle.ld_decode_wait_test.argtypes = [i64, i32]
+    handle.ld_decode_wait_test.restype = i32
     _lib = handle
     return handle
 
@@ -119,6 +121,12 @@ def set_decode_kernel(name: str) -> str:
     if previous < 0:
         raise LightDeltaError(-previous, last_error())
     return {v: k for k, v in DECODE_KERNELS.items()}[previous]
+
+
+def set_decode_wait_test(limit_ns: int = 0, extra_tx_bytes: int = 0) -> None:
+    """Bound of the persistent decode kernel's in-kernel waits (0: the default of one second) and
+    the test-only over-count of each state load's expected bytes (0: off); see ld_decode_wait_test."""
+    check(lib().ld_decode_wait_test(int(limit_ns), int(extra_tx_bytes)))
 
 
 def set_programmatic_launch(enable: bool) -> bool:

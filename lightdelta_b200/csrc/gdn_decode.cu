@@ -101,6 +101,8 @@ struct DecodeArgs {
   int weight_bf16;
   float q_scale;
   float eps;
+  uint64_t wait_ns;   // bound of every in-kernel wait of the persistent kernel (ld_decode_wait_test)
+  uint32_t extra_tx;  // test only: bytes each state load announces beyond what it copies (normally 0)
 };
 
 // The state pool of a launch as the kernel's element type.
@@ -525,7 +527,6 @@ __global__ void __launch_bounds__(Tile<4>::kThreads, 2) gdn_decode_rowreg_kernel
 namespace stream {
 
 constexpr int kStates = 3;                            // fp32 state ring depth (64 KiB each)
-constexpr uint64_t kWaitLimitNs = 1000000000ull;      // 1 s bound on every mbarrier wait
 
 enum ItemKind : int { kSkip = 0, kZero = 1, kRun = 2 };
 
@@ -613,12 +614,12 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-// Waits for the phase of `bar` with the given parity; false once kWaitLimitNs has passed.
-__device__ __noinline__ bool mbar_wait(unsigned long long* bar, uint32_t parity) {
+// Waits for the phase of `bar` with the given parity; false once `limit_ns` have passed.
+__device__ __noinline__ bool mbar_wait(unsigned long long* bar, uint32_t parity, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_ns();
   while (!mbar_try_wait(bar, parity)) {
-    if (global_ns() - start > kWaitLimitNs) return false;
+    if (global_ns() - start > limit_ns) return false;
   }
   return true;
 }
@@ -632,8 +633,8 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 }
 
 // Bounded wait whose outcome is the same for every lane of the warp.
-__device__ __forceinline__ bool warp_wait(unsigned long long* bar, uint32_t parity) {
-  return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+__device__ __forceinline__ bool warp_wait(unsigned long long* bar, uint32_t parity, uint64_t limit_ns) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, limit_ns));
 }
 
 template <class S>
@@ -719,7 +720,7 @@ __device__ bool publish_norms(const DecodeArgs& p, S& sm, int k, int lane) {
   constexpr int kActs = S::kActStages;
   const int s = k % kStates;
   const int a = k % kActs;
-  if (!warp_wait(&sm.full[s], (k / kStates) & 1)) {
+  if (!warp_wait(&sm.full[s], (k / kStates) & 1, p.wait_ns)) {
     if (lane == 0) set_abort(sm);
     return false;
   }
@@ -775,8 +776,8 @@ __device__ void produce(const DecodeArgs& p, S& sm, int lane) {
     const int s = k % kStates;
     const int a = k % kActs;
     bool ok = true;
-    if (k >= kStates) ok = warp_wait(&sm.empty_state[s], ((k / kStates) - 1) & 1);
-    if (ok && k >= kActs) ok = warp_wait(&sm.empty_act[a], ((k / kActs) - 1) & 1);
+    if (k >= kStates) ok = warp_wait(&sm.empty_state[s], ((k / kStates) - 1) & 1, p.wait_ns);
+    if (ok && k >= kActs) ok = warp_wait(&sm.empty_act[a], ((k / kActs) - 1) & 1, p.wait_ns);
     if (!ok) {
       if (lane == 0) set_abort(sm);
       break;
@@ -795,7 +796,7 @@ __device__ void produce(const DecodeArgs& p, S& sm, int lane) {
       if (kind == kRun) {
         using State = typename S::State;
         constexpr uint32_t kStateBytes = kHeadElems * sizeof(State);
-        mbar_arrive_expect_tx(&sm.full[s], kStateBytes + n * 4 * kRowBytes);
+        mbar_arrive_expect_tx(&sm.full[s], kStateBytes + n * 4 * kRowBytes + p.extra_tx);
         const State* src_head =
             state_base<State>(p) + static_cast<int64_t>(src) * p.slot_stride + static_cast<int64_t>(head) * kHeadElems;
         // Four pieces, starting at a per-SM quarter (see store_tile).
@@ -831,7 +832,7 @@ __device__ void produce(const DecodeArgs& p, S& sm, int lane) {
   }
   if (lane == 0) {
     for (int kk = k > kStates ? k - kStates : 0; kk < k; ++kk) {
-      if (!mbar_wait(&sm.full[kk % kStates], (kk / kStates) & 1)) {
+      if (!mbar_wait(&sm.full[kk % kStates], (kk / kStates) & 1, p.wait_ns)) {
         set_abort(sm);
         break;
       }
@@ -882,11 +883,11 @@ __device__ void consume(const DecodeArgs& p, S& sm, int tid) {
   for (int64_t item = blockIdx.x; item < p.total_items; item += gridDim.x, ++k) {
     const int s = k % kStates;
     const int a = k % kActs;
-    if (!warp_wait(&sm.full[s], (k / kStates) & 1)) {
+    if (!warp_wait(&sm.full[s], (k / kStates) & 1, p.wait_ns)) {
       if (lane == 0) set_abort(sm);
       break;
     }
-    if (S::kProducerNorms && !warp_wait(&sm.ready[a], (k / kActs) & 1)) {
+    if (S::kProducerNorms && !warp_wait(&sm.ready[a], (k / kActs) & 1, p.wait_ns)) {
       if (lane == 0) set_abort(sm);
       break;
     }
@@ -920,7 +921,7 @@ __device__ void consume(const DecodeArgs& p, S& sm, int tid) {
     const int buf = runs & 1;
     const int use = runs >> 1;
     // out[buf] was last read by the epilogue two run items ago.
-    if (use > 0 && !warp_wait(&sm.out_empty[buf], (use - 1) & 1)) {
+    if (use > 0 && !warp_wait(&sm.out_empty[buf], (use - 1) & 1, p.wait_ns)) {
       if (lane == 0) set_abort(sm);
       break;
     }
@@ -989,7 +990,7 @@ __device__ void consume(const DecodeArgs& p, S& sm, int tid) {
       mbar_arrive(&sm.out_full[buf]);
     }
     if (et < n) {
-      if (!warp_wait(&sm.out_full[buf], use & 1)) {  // every row's output of this item is in o_buf
+      if (!warp_wait(&sm.out_full[buf], use & 1, p.wait_ns)) {  // every row's output of this item is in o_buf
         if (lane == 0) set_abort(sm);
         break;
       }
@@ -1041,519 +1042,6 @@ __global__ void __maxnreg__(168) gdn_decode_stream_kernel(const DecodeArgs p) {
   }
 }
 
-
-// ------------------------------------------------------------------------------------------
-// TMA-store variant.  The SM's global-store port moves about 61 GB/s, so writing a 64 KiB
-// state from registers occupies the consumer warps for over a microsecond per step, during
-// which their ALUs idle (and during compute the port idles).  Here each step's state is
-// written into a shared-memory staging tile instead and a dedicated storer warp drains it
-// with one TMA bulk store (cp.async.bulk.global.shared::cta) while the consumer warps go on
-// computing.  Two load stages plus the staging tile fit in shared memory.
-// ------------------------------------------------------------------------------------------
-namespace ts {
-
-constexpr int kConsumers = Tile<4>::kThreads;    // 256
-constexpr int kConsumerWarps = kConsumers / 32;  // 8
-constexpr int kThreads = kConsumers + 64;        // + producer warp + storer warp
-
-// kLoads TMA load stages and kStaging staging tiles: (2, 1) for decode, where prefetch depth
-// matters, and (1, 2) for multi-token verify, where each item makes several stores and a second
-// staging tile lets one step's drain overlap the next step's compute.
-template <int kLoads, int kStaging>
-struct Smem {
-  using State = float;
-  static constexpr bool kProducerNorms = false;
-  static constexpr int kStateStages = kLoads;
-  static constexpr int kActStages = kLoads + 1;
-  float state[kLoads][kHeadElems];
-  float staging[kStaging][kHeadElems];
-  ActStage act[kLoads + 1];
-  float out[2][kMaxTokens][kDim];
-  float* store_dst[2];                   // destination of staging event e (entry e & 1); null ends the storer
-  unsigned long long full[kLoads];
-  unsigned long long empty_state[kLoads];
-  unsigned long long empty_act[kLoads + 1];
-  unsigned long long out_full[2];
-  unsigned long long out_empty[2];
-  unsigned long long tile_ready[kStaging];    // every consumer warp has written its part of the tile
-  unsigned long long staging_free[kStaging];  // the storer's bulk store has read the tile out
-  int abort;
-};
-
-template <int kLoads, int kStaging>
-__device__ void consume(const DecodeArgs& p, Smem<kLoads, kStaging>& sm, int tid) {
-  constexpr int kRows = 4;
-  constexpr int kRowGroups = Tile<kRows>::kRowGroups;
-  constexpr int kActRing = kLoads + 1;
-  const int HV = p.num_v_heads;
-  const int lane = tid & 31;
-  const int warp = tid >> 5;
-  const int j = tid & (kLanesPerRow - 1);
-  const int g = tid / kLanesPerRow;
-  float w[4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) w[e] = load_param(p.weight, 4 * lane + e, p.weight_bf16);
-  int k = 0;
-  int runs = 0;
-  uint32_t events = 0;  // staging events issued (same count in every consumer warp)
-  bool failed = false;
-  for (int64_t item = blockIdx.x; item < p.total_items; item += gridDim.x, ++k) {
-    const int s = k % kLoads;
-    const int a = k % kActRing;
-    if (!warp_wait(&sm.full[s], (k / kLoads) & 1)) {
-      failed = true;
-      break;
-    }
-    const ItemInfo& info = sm.act[a].info;
-    const int kind = info.kind;
-    const int n = info.n;
-    const int64_t bos = info.bos;
-    const int head = static_cast<int>(item % HV);
-    if (kind != kRun) {
-      if (kind == kZero) {
-        for (int idx = tid; idx < n * kDim; idx += kConsumers) {
-          const int64_t token = bos + idx / kDim;
-          p.out[(token * HV + head) * kDim + (idx % kDim)] = __float2bfloat16_rn(0.0f);
-        }
-      }
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&sm.empty_state[s]);
-        mbar_arrive(&sm.empty_act[a]);
-      }
-      continue;
-    }
-
-    float4 tile[kRows][kVecPerRow];
-    load_tile<kRows>(sm.state[s], g, j, tile);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.empty_state[s]);
-
-    const ActStage& act = sm.act[a];
-    const int buf = runs & 1;
-    const int use = runs >> 1;
-    if (use > 0 && !warp_wait(&sm.out_empty[buf], (use - 1) & 1)) {
-      failed = true;
-      break;
-    }
-    float* o_buf = &sm.out[buf][0][0];
-    const int64_t head_offset = static_cast<int64_t>(head) * kHeadElems;
-    for (int t = 0; t < n; ++t) {
-      float4 kv[kVecPerRow], qv[kVecPerRow];
-      float k_sq, q_sq;
-      load_row_cols<false>(act.k[t], j, kv, k_sq);
-      load_row_cols<false>(act.q[t], j, qv, q_sq);
-      k_sq = row_sum(k_sq);
-      q_sq = row_sum(q_sq);
-      // L2 norm in fp32 as gdn.py:98-99; q then scaled by K^-1/2 as gdn.py:101.
-      const float k_inv = 1.0f / sqrtf(k_sq + 1e-6f);
-      const float q_inv = 1.0f / sqrtf(q_sq + 1e-6f);
-#pragma unroll
-      for (int c = 0; c < kVecPerRow; ++c) {
-        kv[c] = make_float4(kv[c].x * k_inv, kv[c].y * k_inv, kv[c].z * k_inv, kv[c].w * k_inv);
-        qv[c] = make_float4(qv[c].x * q_inv * p.q_scale, qv[c].y * q_inv * p.q_scale, qv[c].z * q_inv * p.q_scale,
-                            qv[c].w * q_inv * p.q_scale);
-      }
-      float vrow[kRows], o[kRows];
-#pragma unroll
-      for (int i = 0; i < kRows; ++i) vrow[i] = __bfloat162float(act.v[t][g + i * kRowGroups]);
-      tile_step<kRows>(tile, kv, qv, vrow, info.decay[t], info.beta[t], o);
-      if (j == 0) {
-#pragma unroll
-        for (int i = 0; i < kRows; ++i) o_buf[t * kDim + g + i * kRowGroups] = __bfloat162float(__float2bfloat16_rn(o[i]));
-      }
-      const int dst = info.dst[t];
-      if (dst > 0) {
-        // Staging tile b is free once the storer has read out event `events - kStaging`.
-        const int b = events % kStaging;
-        if (events >= kStaging && !warp_wait(&sm.staging_free[b], ((events / kStaging) - 1) & 1)) {
-          failed = true;
-          break;
-        }
-        store_tile<kRows>(sm.staging[b], g, j, tile);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> TMA reads
-        if (tid == 0) sm.store_dst[events & 1] = p.state + static_cast<int64_t>(dst) * p.slot_stride + head_offset;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.tile_ready[b]);
-        ++events;
-      }
-    }
-    if (failed) break;
-    // The epilogue of token t of this item runs on warp (runs + t) mod 8, spreading the
-    // gated-RMSNorm work over all consumer warps instead of loading warp 0 with every token.
-    const int my_token = (warp - runs % kConsumerWarps + kConsumerWarps) % kConsumerWarps;
-    const bool epilogue = my_token < n;
-    float z[4] = {0.f, 0.f, 0.f, 0.f};
-    if (epilogue) {
-      const uint2 raw = *reinterpret_cast<const uint2*>(&act.z[my_token][4 * lane]);
-      z[0] = bf16_lo(raw.x);
-      z[1] = bf16_hi(raw.x);
-      z[2] = bf16_lo(raw.y);
-      z[3] = bf16_hi(raw.y);
-    }
-    __syncwarp();
-    if (lane == 0) {
-      mbar_arrive(&sm.empty_act[a]);
-      mbar_arrive(&sm.out_full[buf]);
-    }
-    if (epilogue) {
-      if (!warp_wait(&sm.out_full[buf], use & 1)) {  // every row's output of this item is in o_buf
-        failed = true;
-        break;
-      }
-      gated_rmsnorm_store<true>(o_buf + my_token * kDim, z, w, p.eps, lane,
-                                p.out + ((bos + my_token) * HV + head) * kDim);
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.out_empty[buf]);
-    ++runs;
-  }
-  if (failed) {
-    if (lane == 0) set_abort(sm);
-    return;
-  }
-  // A final staging event with a null destination tells the storer to finish.
-  if (events >= kStaging &&
-      !warp_wait(&sm.staging_free[events % kStaging], ((events / kStaging) - 1) & 1)) {
-    if (lane == 0) set_abort(sm);
-    return;
-  }
-  if (tid == 0) sm.store_dst[events & 1] = nullptr;
-  __syncwarp();
-  if (lane == 0) mbar_arrive(&sm.tile_ready[events % kStaging]);
-}
-
-// Storer warp (one lane): drains staging event e with a TMA bulk store of tile e % kStaging.
-// With two tiles it keeps one store in flight while waiting for the next tile.
-template <int kLoads, int kStaging>
-__device__ void store_loop(Smem<kLoads, kStaging>& sm, int lane) {
-  if (lane != 0) return;
-  uint32_t e = 0;
-  for (;; ++e) {
-    const int b = e % kStaging;
-    if (!mbar_wait(&sm.tile_ready[b], (e / kStaging) & 1)) {
-      set_abort(sm);
-      break;
-    }
-    float* dst = sm.store_dst[e & 1];
-    if (dst == nullptr) break;
-    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_u32(sm.staging[b])),
-                 "r"(kHeadBytes)
-                 : "memory");
-    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-    if constexpr (kStaging == 1) {
-      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-      mbar_arrive(&sm.staging_free[0]);
-    } else {
-      // Event e - 1 has been read out once at most one group (event e) is still reading.
-      if (e > 0) {
-        asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-        mbar_arrive(&sm.staging_free[(e - 1) % kStaging]);
-      }
-    }
-  }
-  if constexpr (kStaging > 1) {
-    if (e > 0) {
-      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-      mbar_arrive(&sm.staging_free[(e - 1) % kStaging]);
-    }
-  }
-  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // every bulk store has completed
-}
-
-// Block: 256 consumer threads, one producer warp, one storer warp; one CTA per SM.
-template <int kLoads, int kStaging>
-__global__ void __maxnreg__(168) gdn_decode_tmastore_kernel(const DecodeArgs p) {
-  ldb::grid_dependency_wait();
-  ldb::allow_dependent_launch();
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  using S = Smem<kLoads, kStaging>;
-  S& sm = *reinterpret_cast<S*>(smem_raw);
-  const int tid = threadIdx.x;
-  if (tid == 0) {
-    for (int s = 0; s < kLoads; ++s) {
-      mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty_state[s], kConsumerWarps);
-    }
-    for (int a = 0; a < kLoads + 1; ++a) mbar_init(&sm.empty_act[a], kConsumerWarps);
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&sm.out_full[b], kConsumerWarps);
-      mbar_init(&sm.out_empty[b], kConsumerWarps);
-    }
-    for (int b = 0; b < kStaging; ++b) {
-      mbar_init(&sm.tile_ready[b], kConsumerWarps);
-      mbar_init(&sm.staging_free[b], 1);
-    }
-    sm.abort = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  }
-  __syncthreads();
-  if (tid < kConsumers) {
-    consume<kLoads, kStaging>(p, sm, tid);
-  } else if (tid < kConsumers + 32) {
-    produce(p, sm, tid & 31);
-  } else {
-    store_loop<kLoads, kStaging>(sm, tid & 31);
-  }
-}
-
-}  // namespace ts
-
-
-// ------------------------------------------------------------------------------------------
-// Staged kernel: one item split across a cluster of Q CTAs.  Each CTA owns 128/Q rows of the
-// (request, head) state, TMA-loads that row slice (64/Q KiB) and the item's activation rows into
-// shared memory, and runs the recurrence on a small register tile in row passes (rows are
-// independent until the output norm).  The gated RMSNorm needs all 128 outputs of a token: each
-// CTA reduces its rows' sum of squares and, for Q > 1, reads its peers' partial sums through
-// distributed shared memory.  Shared memory rather than registers holds the in-flight state, so
-// three CTAs per SM keep up to 192 KiB of loads in flight (Q = 1); Q = 2 or 4 spreads small
-// batches over more SMs.  Every CTA of a cluster takes the same path, so all reach its barriers.
-// ------------------------------------------------------------------------------------------
-namespace staged {
-
-constexpr int kThreads = 256;
-constexpr int kRowGroups = kThreads / kLanesPerRow;  // 32
-
-template <int Q>
-struct Shape {
-  static constexpr int kRowsPerCta = kDim / Q;                        // 128, 64, 32
-  static constexpr int kRowsPerThread = kRowsPerCta >= 64 ? 2 : 1;   // rows per thread per pass
-  static constexpr int kPasses = kRowsPerCta / (kRowGroups * kRowsPerThread);
-  static constexpr int kValuesPerLane = kRowsPerCta / 32;            // epilogue rows per lane
-};
-
-template <int Q>
-struct Smem {
-  float state[Shape<Q>::kRowsPerCta * kDim];
-  __nv_bfloat16 q[kMaxTokens][kDim];
-  __nv_bfloat16 k[kMaxTokens][kDim];
-  __nv_bfloat16 v[kMaxTokens][Shape<Q>::kRowsPerCta];
-  __nv_bfloat16 z[kMaxTokens][Shape<Q>::kRowsPerCta];
-  float o[kMaxTokens][Shape<Q>::kRowsPerCta];
-  float partial[kMaxTokens];
-  int dst[kMaxTokens];
-  float decay[kMaxTokens];
-  float beta[kMaxTokens];
-  int kind;
-  int n;
-  int bos;
-  unsigned long long full;
-};
-
-__device__ __forceinline__ unsigned int cluster_rank() {
-  unsigned int r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
-}
-
-// Reads a float from the same shared-memory offset in CTA `rank` of this cluster.
-__device__ __forceinline__ float peer_load(const float* local, unsigned int rank) {
-  uint32_t remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
-  float value;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(value) : "r"(remote) : "memory");
-  return value;
-}
-
-template <int Q>
-__device__ __forceinline__ void staged_body(const DecodeArgs& p, Smem<Q>& sm) {
-  using S = Shape<Q>;
-  constexpr int kRows = S::kRowsPerThread;
-  const int HV = p.num_v_heads;
-  const int W = p.width;
-  const int tid = threadIdx.x;
-  const int lane = tid & 31;
-  const int warp = tid >> 5;
-  const int j = tid & (kLanesPerRow - 1);
-  const int g = tid / kLanesPerRow;
-  const int64_t item = blockIdx.x / Q;
-  const unsigned int rank = Q > 1 ? cluster_rank() : 0u;
-  const int row0 = static_cast<int>(rank) * S::kRowsPerCta;
-  const int request = static_cast<int>(item / HV);
-  const int head = static_cast<int>(item - static_cast<int64_t>(request) * HV);
-
-  // Metadata (warp 0), then the TMA loads of this CTA's share of the item (thread 0).
-  if (warp == 0) {
-    const int bos = p.cu[request];
-    const int eos = p.cu[request + 1];
-    const int n = eos - bos;
-    int kind = kRun;
-    int src = 0;
-    if (n <= 0) {
-      kind = kSkip;
-    } else if (bos < 0 || static_cast<int64_t>(eos) > p.n_tokens) {
-      kind = kSkip;
-      if (lane == 0 && rank == 0) atomicOr(&g_decode_faults, LD_FAULT_DECODE_TOKENS);
-    } else {
-      const int acc = p.accepted[request];
-      src = (acc >= 1 && acc <= W) ? p.indices[request * W + acc - 1] : 0;
-      if (src <= 0 || n > W || src >= p.n_slots) {
-        kind = kZero;
-        if (lane == 0 && rank == 0) {
-          if (n > W) atomicOr(&g_decode_faults, LD_FAULT_DECODE_TOKENS);
-          if (src >= p.n_slots) atomicOr(&g_decode_faults, LD_FAULT_DECODE_SLOT_RANGE);
-        }
-      }
-    }
-    if (kind == kRun && lane < n) {
-      int dst = p.indices[request * W + lane];
-      if (dst >= p.n_slots) {
-        if (rank == 0) atomicOr(&g_decode_faults, LD_FAULT_DECODE_SLOT_RANGE);
-        dst = 0;
-      }
-      sm.dst[lane] = dst;
-      token_gates(p, bos + lane, head, sm.decay[lane], sm.beta[lane]);
-    }
-    if (lane == 0) {
-      sm.kind = kind;
-      sm.n = n;
-      sm.bos = bos;
-      mbar_init(&sm.full, 1);
-      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      if (kind == kRun) {
-        const int H = p.num_k_heads;
-        const int key_head = head / p.heads_ratio;
-        mbar_arrive_expect_tx(&sm.full, S::kRowsPerCta * kDim * 4 + n * (2 * kRowBytes + 4 * S::kRowsPerCta));
-        bulk_load(sm.state,
-                  p.state + static_cast<int64_t>(src) * p.slot_stride + static_cast<int64_t>(head) * kHeadElems +
-                      static_cast<int64_t>(row0) * kDim,
-                  S::kRowsPerCta * kDim * 4, &sm.full);
-        for (int t = 0; t < n; ++t) {
-          const int64_t token = bos + t;
-          const __nv_bfloat16* row = p.qkv + token * p.qkv_row;
-          bulk_load(sm.q[t], row + key_head * kDim, kRowBytes, &sm.full);
-          bulk_load(sm.k[t], row + (H + key_head) * kDim, kRowBytes, &sm.full);
-          bulk_load(sm.v[t], row + (2 * H + head) * kDim + row0, 2 * S::kRowsPerCta, &sm.full);
-          bulk_load(sm.z[t], p.gate + token * p.gate_row + head * kDim + row0, 2 * S::kRowsPerCta, &sm.full);
-        }
-      }
-    }
-  }
-  __syncthreads();
-  const int kind = sm.kind;
-  const int n = sm.n;
-  const int64_t bos = sm.bos;
-  if (kind == kSkip) return;  // the same for every CTA of the cluster
-  if (kind == kZero) {
-    for (int idx = tid; idx < n * S::kRowsPerCta; idx += kThreads) {
-      const int64_t token = bos + idx / S::kRowsPerCta;
-      p.out[(token * HV + head) * kDim + row0 + (idx % S::kRowsPerCta)] = __float2bfloat16_rn(0.0f);
-    }
-    return;
-  }
-  if (!mbar_wait(&sm.full, 0)) {
-    // The loads did not land in time: report, and keep the cluster's control flow intact.
-    if (tid == 0) atomicOr(&g_decode_faults, LD_FAULT_WAIT_TIMEOUT);
-  }
-
-  const int64_t head_offset = static_cast<int64_t>(head) * kHeadElems;
-#pragma unroll 1
-  for (int pass = 0; pass < S::kPasses; ++pass) {
-    const int pass_row = pass * kRowGroups * kRows;  // first local row of this pass
-    float4 tile[kRows][kVecPerRow];
-    {
-      const float4* src4 = reinterpret_cast<const float4*>(sm.state + (pass_row + g) * kDim + 4 * j);
-#pragma unroll
-      for (int i = 0; i < kRows; ++i) {
-#pragma unroll
-        for (int c = 0; c < kVecPerRow; ++c) tile[i][c] = src4[(i * kRowGroups * kDim + c * 4 * kLanesPerRow) / 4];
-      }
-    }
-    for (int t = 0; t < n; ++t) {
-      float4 kv[kVecPerRow], qv[kVecPerRow];
-      float k_sq, q_sq;
-      load_row_cols<false>(sm.k[t], j, kv, k_sq);
-      load_row_cols<false>(sm.q[t], j, qv, q_sq);
-      k_sq = row_sum(k_sq);
-      q_sq = row_sum(q_sq);
-      // L2 norm in fp32 as gdn.py:98-99; q then scaled by K^-1/2 as gdn.py:101.
-      const float k_inv = 1.0f / sqrtf(k_sq + 1e-6f);
-      const float q_inv = 1.0f / sqrtf(q_sq + 1e-6f);
-#pragma unroll
-      for (int c = 0; c < kVecPerRow; ++c) {
-        kv[c] = make_float4(kv[c].x * k_inv, kv[c].y * k_inv, kv[c].z * k_inv, kv[c].w * k_inv);
-        qv[c] = make_float4(qv[c].x * q_inv * p.q_scale, qv[c].y * q_inv * p.q_scale, qv[c].z * q_inv * p.q_scale,
-                            qv[c].w * q_inv * p.q_scale);
-      }
-      float vrow[kRows], o[kRows];
-#pragma unroll
-      for (int i = 0; i < kRows; ++i) vrow[i] = __bfloat162float(sm.v[t][pass_row + g + i * kRowGroups]);
-      tile_step<kRows>(tile, kv, qv, vrow, sm.decay[t], sm.beta[t], o);
-      if (j == 0) {
-#pragma unroll
-        for (int i = 0; i < kRows; ++i) {
-          // The recurrence output is rounded to bf16 before the norm (gdn.py:116).
-          sm.o[t][pass_row + g + i * kRowGroups] = __bfloat162float(__float2bfloat16_rn(o[i]));
-        }
-      }
-      const int dst = sm.dst[t];
-      if (dst > 0) {
-        float4* out4 = reinterpret_cast<float4*>(p.state + static_cast<int64_t>(dst) * p.slot_stride + head_offset +
-                                                 static_cast<int64_t>(row0 + pass_row + g) * kDim + 4 * j);
-#pragma unroll
-        for (int i = 0; i < kRows; ++i) {
-#pragma unroll
-          for (int c = 0; c < kVecPerRow; ++c) out4[(i * kRowGroups * kDim + c * 4 * kLanesPerRow) / 4] = tile[i][c];
-        }
-      }
-    }
-  }
-  __syncthreads();  // every local row's output is in sm.o
-
-  // Gated RMSNorm (gdn.py:117-119): warp t normalises token t over all 128 rows of the head.
-  constexpr int E = S::kValuesPerLane;
-  float ov[E];
-  float sq = 0.0f;  // after warp_sum: this CTA's sum of squares of token `warp`, in every lane
-  if (warp < n) {
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-      ov[e] = sm.o[warp][E * lane + e];
-      sq += ov[e] * ov[e];
-    }
-    sq = warp_sum(sq);
-    if (Q > 1 && lane == 0) sm.partial[warp] = sq;
-  }
-  if constexpr (Q > 1) cluster_sync();  // every CTA's partial sums are visible cluster-wide
-  if (warp < n) {
-    float total = sq;
-    if constexpr (Q > 1) {
-      // Summed in rank order by every CTA of the cluster, so all of them use the same value.
-      total = 0.0f;
-#pragma unroll
-      for (int r = 0; r < Q; ++r) total += peer_load(&sm.partial[warp], r);
-    }
-    const float rstd = 1.0f / sqrtf(total / static_cast<float>(kDim) + p.eps);
-    const int64_t token = bos + warp;
-    __nv_bfloat16* out_row = p.out + (token * HV + head) * kDim + row0 + E * lane;
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-      const int row = row0 + E * lane + e;
-      const float z = __bfloat162float(sm.z[warp][E * lane + e]);
-      const float silu = z / (1.0f + expf(-z));
-      const float w = load_param(p.weight, row, p.weight_bf16);
-      out_row[e] = __float2bfloat16_rn(ov[e] * rstd * w * silu);
-    }
-  }
-  if constexpr (Q > 1) cluster_sync();  // no CTA leaves while a peer may still read its partials
-}
-
-template <int Q>
-__global__ void __cluster_dims__(Q, 1, 1) __launch_bounds__(kThreads, 3) gdn_decode_staged_kernel(const DecodeArgs p) {
-  ldb::grid_dependency_wait();
-  ldb::allow_dependent_launch();
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  staged_body<Q>(p, *reinterpret_cast<Smem<Q>*>(smem_raw));
-}
-
-}  // namespace staged
-
 }  // namespace stream
 
 bool aligned(const void* ptr, uintptr_t bytes) { return (reinterpret_cast<uintptr_t>(ptr) % bytes) == 0; }
@@ -1586,29 +1074,6 @@ int device_info(DeviceInfo& out) {
                                  static_cast<int>(sizeof(stream::SmemT<__nv_bfloat16>)));
     }
     if (err != cudaSuccess) return set_error(LD_ERR_CUDA, "shared-memory opt-in: %s", cudaGetErrorString(err));
-    err = cudaFuncSetAttribute(stream::ts::gdn_decode_tmastore_kernel<2, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(sizeof(stream::ts::Smem<2, 1>)));
-    if (err == cudaSuccess) {
-      err = cudaFuncSetAttribute(stream::ts::gdn_decode_tmastore_kernel<1, 2>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(sizeof(stream::ts::Smem<1, 2>)));
-    }
-    if (err == cudaSuccess) {
-      err = cudaFuncSetAttribute(stream::staged::gdn_decode_staged_kernel<1>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(sizeof(stream::staged::Smem<1>)));
-    }
-    if (err == cudaSuccess) {
-      err = cudaFuncSetAttribute(stream::staged::gdn_decode_staged_kernel<2>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(sizeof(stream::staged::Smem<2>)));
-    }
-    if (err == cudaSuccess) {
-      err = cudaFuncSetAttribute(stream::staged::gdn_decode_staged_kernel<4>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(sizeof(stream::staged::Smem<4>)));
-    }
-    if (err != cudaSuccess) return set_error(LD_ERR_CUDA, "shared-memory opt-in: %s", cudaGetErrorString(err));
     info.stream_ready = true;
   }
   out = info;
@@ -1616,6 +1081,9 @@ int device_info(DeviceInfo& out) {
 }
 
 std::atomic<int> g_kernel_override{LD_DECODE_KERNEL_AUTO};
+constexpr uint64_t kDefaultWaitNs = 1000000000ull;  // 1 s bound on every in-kernel wait
+std::atomic<uint64_t> g_wait_ns{kDefaultWaitNs};
+std::atomic<uint32_t> g_extra_tx{0};
 
 }  // namespace
 
@@ -1721,6 +1189,8 @@ int prepare_decode(const void* qkv, int64_t qkv_row_stride, const void* a, int64
   // K^-1/2 evaluated in double and rounded once, as torch scales an fp32 tensor by a Python float.
   args.q_scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(LD_HEAD_DIM)));
   args.eps = eps;
+  args.wait_ns = g_wait_ns.load(std::memory_order_relaxed);
+  args.extra_tx = g_extra_tx.load(std::memory_order_relaxed);
   return ok();
 }
 
@@ -1761,30 +1231,10 @@ extern "C" int ld_decode(const void* qkv, int64_t qkv_row_stride, const void* a,
                                                                               : LD_DECODE_KERNEL_ROWREG;
   }
   cudaError_t err;
-  if (variant != LD_DECODE_KERNEL_ROWREG) {
+  if (variant == LD_DECODE_KERNEL_STREAM) {
     const dim3 grid(static_cast<unsigned int>(std::min<int64_t>(args.total_items, info.sms)));
-    const dim3 items(static_cast<unsigned int>(args.total_items));
-    if (variant == LD_DECODE_KERNEL_STAGED_Q1) {
-      err = ldb::launch(stream::staged::gdn_decode_staged_kernel<1>, items, dim3(stream::staged::kThreads),
-                        sizeof(stream::staged::Smem<1>), s, 1, args);
-    } else if (variant == LD_DECODE_KERNEL_STAGED_Q2) {
-      err = ldb::launch(stream::staged::gdn_decode_staged_kernel<2>, dim3(2 * items.x), dim3(stream::staged::kThreads),
-                        sizeof(stream::staged::Smem<2>), s, 1, args);
-    } else if (variant == LD_DECODE_KERNEL_STAGED_Q4) {
-      err = ldb::launch(stream::staged::gdn_decode_staged_kernel<4>, dim3(4 * items.x), dim3(stream::staged::kThreads),
-                        sizeof(stream::staged::Smem<4>), s, 1, args);
-    } else if (variant == LD_DECODE_KERNEL_TMA_STORE) {
-      if (width == 1) {
-        err = ldb::launch(stream::ts::gdn_decode_tmastore_kernel<2, 1>, grid, dim3(stream::ts::kThreads),
-                          sizeof(stream::ts::Smem<2, 1>), s, 1, args);
-      } else {
-        err = ldb::launch(stream::ts::gdn_decode_tmastore_kernel<1, 2>, grid, dim3(stream::ts::kThreads),
-                          sizeof(stream::ts::Smem<1, 2>), s, 1, args);
-      }
-    } else {
-      err = ldb::launch(stream::gdn_decode_stream_kernel<4, float>, grid, dim3(Tile<4>::kThreads + 32),
-                        sizeof(stream::Smem), s, 1, args);
-    }
+    err = ldb::launch(stream::gdn_decode_stream_kernel<4, float>, grid, dim3(Tile<4>::kThreads + 32),
+                      sizeof(stream::Smem), s, 1, args);
   } else {
     const bool vec_act = aligned(qkv, 8) && qkv_row_stride % 4 == 0 && aligned(gate, 8) &&
                          gate_row_stride % 4 == 0 && aligned(out, 8);
@@ -1801,8 +1251,17 @@ extern "C" int ld_decode(const void* qkv, int64_t qkv_row_stride, const void* a,
   return ok();
 }
 
+extern "C" int ld_decode_wait_test(int64_t limit_ns, int32_t extra_tx_bytes) {
+  if (limit_ns < 0 || extra_tx_bytes < 0 || extra_tx_bytes > 1024) {
+    return ldb::set_error(LD_ERR_INVALID, "ld_decode_wait_test: limit_ns >= 0 and 0 <= extra_tx_bytes <= 1024");
+  }
+  ldb::g_wait_ns.store(limit_ns == 0 ? ldb::kDefaultWaitNs : static_cast<uint64_t>(limit_ns));
+  ldb::g_extra_tx.store(static_cast<uint32_t>(extra_tx_bytes));
+  return ldb::ok();
+}
+
 extern "C" int ld_decode_kernel_override(int variant) {
-  if (variant < LD_DECODE_KERNEL_AUTO || variant > LD_DECODE_KERNEL_STAGED_Q4) {
+  if (variant < LD_DECODE_KERNEL_AUTO || variant > LD_DECODE_KERNEL_STREAM) {
     return ldb::set_error(-LD_ERR_INVALID, "unknown decode kernel variant %d", variant);
   }
   return ldb::g_kernel_override.exchange(variant);

@@ -140,6 +140,13 @@ def test_process_wide_toggles(native):
     assert lib.ld_programmatic_launch(-1) == enabled
 
 
+def test_wait_test_hook_checks_its_arguments(native):
+    lib = native.lib()
+    assert lib.ld_decode_wait_test(-1, 0) == native.LD_ERR_INVALID
+    assert lib.ld_decode_wait_test(0, 4096) == native.LD_ERR_INVALID
+    assert lib.ld_decode_wait_test(0, 0) == native.LD_OK
+
+
 def test_loads_as_the_reference_package_extension(native, tmp_path):
     """The drop-in route of the reference's loader (python/lightdelta/ops/__init__.py:7 finds
     `lightdelta._C` with importlib and loads it with torch.ops.load_library): with the two

@@ -21,7 +21,7 @@ from lightdelta_b200.config import BackendConfig
 
 pytestmark = pytest.mark.gpu
 
-VARIANTS = ["auto", "stream", "rowreg", "tmastore", "staged1", "staged2", "staged4"]
+VARIANTS = ["auto", "stream", "rowreg"]
 
 
 @pytest.fixture(params=VARIANTS)

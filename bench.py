@@ -19,9 +19,13 @@ Workloads (the default is the one the headline metric is quote
 A step is one launch of the op over that batch.  Under torchrun every rank runs the same
 per-GPU workload on its own slot shard (weak scaling, no data-path collective); the
 rank-local device times are combined as their maximum.  Rank 0 prints one JSON line.
+The default (decode) line also carries `extra`: configs 3 (verify) and 4 (copy) and both decode
+configs on a bf16 state pool, each timed the same way after the headline (--no-extras skips them).
 
 --impl reference times the CPU oracle port (oracle/, all host threads) on the same workload and
-metric; under torchrun only rank 0 runs it.
+metric; under torchrun only rank 0 runs it.  When a GPU and the reference harness
+(oracle/_ref/libref_harness.so) are present it also times the reference's own CUDA kernel at the
+BASELINE geometry (HV=32) on configs 2 and 3 (`reference_gpu_kernel`).
 """
 
 from __future__ import annotations
@@ -60,11 +64,14 @@ def parse_args(argv=None):
     p.add_argument("--workload", choices=("decode", "verify", "decode_bf16", "verify_bf16", "commit", "sample", "conv",
                                           "copy", "stacked"),
                    default="decode")
-    p.add_argument("--e2e-steps", type=int, default=200)
-    p.add_argument("--decode-kernel", choices=("auto", "stream", "rowreg", "tmastore", "staged1", "staged2", "staged4"), default="auto",
+    p.add_argument("--e2e-steps", type=int, default=200,
+                   help="steps of the end-to-end (host buffers) measurement, independent of --steps")
+    p.add_argument("--decode-kernel", choices=("auto", "stream", "rowreg"), default="auto",
                    help="decode kernel variant (all compute the same results)")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline budget (rank 0, N=1)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-extras", action="store_true",
+                   help="skip the secondary configs (3, 4, bf16 pool) that the default decode line also reports")
     args = p.parse_args(argv)
     if args.warmup < 3:
         p.error("--warmup must be at least 3")
@@ -218,59 +225,55 @@ def timed_launches(fn, steps: int, warmup: int, dist: Dist, stream):
     return total_ms, total_ms / steps, (wall0, wall1)
 
 
-def run_ours(args, dist: Dist) -> dict | None:
+class Workload:
+    """One timed unit of the bench: `fn` runs one step; the byte and unit counts feed the roofline."""
+
+    def __init__(self, fn, bytes_per_launch, touched, units_per_step, unit, config, *, case=None,
+                 launches_per_step=1, kernels_per_step=None, dtype="fp32", cleanup=None):
+        self.fn = fn
+        self.bytes_per_launch = bytes_per_launch
+        self.touched = touched
+        self.units_per_step = units_per_step
+        self.unit = unit
+        self.config = config
+        self.case = case
+        self.launches_per_step = launches_per_step
+        self.kernels_per_step = launches_per_step if kernels_per_step is None else kernels_per_step
+        self.dtype = dtype
+        self.cleanup = cleanup
+
+
+def build_workload(name: str, args, dist: Dist, device, stream) -> Workload:
     import torch
 
-    from lightdelta_b200 import capi, ops  # noqa: F401
     from lightdelta_b200 import workloads
 
-    capi.set_decode_kernel(args.decode_kernel)
-    torch.cuda.set_device(dist.local_rank)
-    device = torch.device("cuda", dist.local_rank)
-    stream = torch.cuda.current_stream(device)
-    sampler = ClockSampler(device.index if device.index is not None else 0)
-    peaks = measured_peaks()
     seed = 1000 * dist.rank
-
-    if args.workload in ("decode", "verify"):
-        case = workloads.config2(device, seed=2 + seed) if args.workload == "decode" else workloads.config3(
-            device, seed=3 + seed)
-        op_args = case.op_args()
-        requests, width = case.slots.shape
-        tokens = case.tokens
-        hv, h = case.num_v_heads, case.num_k_heads
-        bytes_per_launch = workloads.decode_algorithmic_bytes(requests, width, tokens, h, hv)
-        touched = requests * (1 + width) * hv * workloads.SLOT_HEAD_BYTES
-
-        def fn():
-            torch.ops.lightdelta.decode(*op_args)
-
-        units_per_step, unit = tokens, "tokens/s"
-        config = {"workload": f"config{'2' if args.workload == 'decode' else '3'}_{args.workload}",
-                  "sequences_per_gpu": requests, "tokens_per_sequence": width, "num_k_heads": h,
-                  "num_v_heads": hv, "head_dim": 128, "pool_slots": case.pool.shape[0],
-                  "state_dtype": "fp32", "activation_dtype": "bf16", "decode_kernel": args.decode_kernel}
-    elif args.workload in ("decode_bf16", "verify_bf16"):
-        # The same batches on a bf16 state pool (fp32 recurrence, each stored step rounded).
-        one_token = args.workload == "decode_bf16"
+    if name in ("decode", "verify", "decode_bf16", "verify_bf16"):
+        one_token = name in ("decode", "decode_bf16")
+        bf16_pool = name.endswith("_bf16")
         case = workloads.config2(device, seed=2 + seed) if one_token else workloads.config3(device, seed=3 + seed)
-        case.pool = case.pool.to(torch.bfloat16)
+        if bf16_pool:
+            # The same batches on a bf16 state pool (fp32 recurrence, each stored step rounded).
+            case.pool = case.pool.to(torch.bfloat16)
         op_args = case.op_args()
         requests, width = case.slots.shape
-        tokens = case.tokens
         hv, h = case.num_v_heads, case.num_k_heads
-        bytes_per_launch = workloads.decode_algorithmic_bytes(requests, width, tokens, h, hv, state_itemsize=2)
-        touched = requests * (1 + width) * hv * workloads.SLOT_HEAD_BYTES // 2
+        itemsize = 2 if bf16_pool else 4
+        op = torch.ops.lightdelta.decode_bf16_state if bf16_pool else torch.ops.lightdelta.decode
 
         def fn():
-            torch.ops.lightdelta.decode_bf16_state(*op_args)
+            op(*op_args)
 
-        units_per_step, unit = tokens, "tokens/s"
-        config = {"workload": f"config{'2' if one_token else '3'}_{args.workload}",
-                  "sequences_per_gpu": requests, "tokens_per_sequence": width, "num_k_heads": h,
-                  "num_v_heads": hv, "head_dim": 128, "pool_slots": case.pool.shape[0],
-                  "state_dtype": "bf16", "activation_dtype": "bf16", "decode_kernel": args.decode_kernel}
-    elif args.workload == "commit":
+        config = {"workload": f"config{'2' if one_token else '3'}_{name}", "sequences_per_gpu": requests,
+                  "tokens_per_sequence": width, "num_k_heads": h, "num_v_heads": hv, "head_dim": 128,
+                  "pool_slots": case.pool.shape[0], "state_dtype": "bf16" if bf16_pool else "fp32",
+                  "activation_dtype": "bf16", "decode_kernel": args.decode_kernel}
+        return Workload(fn, workloads.decode_algorithmic_bytes(requests, width, case.tokens, h, hv,
+                                                               state_itemsize=itemsize),
+                        requests * (1 + width) * hv * workloads.SLOT_HEAD_BYTES * itemsize // 4, case.tokens,
+                        "tokens/s", config, case=case, dtype="fp32 (bf16 state pool)" if bf16_pool else "fp32")
+    if name == "commit":
         # Config 3's explicit commit: after verify, copy each sequence's accepted step state to
         # its home slot (the first of its candidate slots) with the pool-to-pool copy op.
         # Four independent config-3 batches on one 1025-slot pool, used in turn, so that the
@@ -292,39 +295,37 @@ def run_ours(args, dist: Dist) -> dict | None:
 
         moved_per_set = [int((src != dst).sum().item()) for src, dst in sets]
         moved = sum(moved_per_set) / 4
-        bytes_per_launch = moved * 2 * first.num_v_heads * workloads.SLOT_HEAD_BYTES
-        touched = sum(moved_per_set) * 2 * first.num_v_heads * workloads.SLOT_HEAD_BYTES
-        units_per_step, unit = first.slots.shape[0], "sequences/s"
-        case = None
         config = {"workload": "config3_commit_copy", "sequences_per_gpu": first.slots.shape[0],
                   "slots_copied_per_step": moved, "pool_slots": pool.shape[0], "batches_in_turn": 4,
                   "note": "a sequence whose accepted slot is its home slot copies nothing"}
-    elif args.workload == "conv":
+        return Workload(fn, moved * 2 * first.num_v_heads * workloads.SLOT_HEAD_BYTES,
+                        sum(moved_per_set) * 2 * first.num_v_heads * workloads.SLOT_HEAD_BYTES,
+                        first.slots.shape[0], "sequences/s", config, dtype="fp32 (bit copy)")
+    if name == "conv":
         case = workloads.config2(device, seed=2 + seed)
         conv = workloads.make_conv_state(case, case.pool.shape[0], seed=7 + seed)
         fused_args = workloads.conv_decode_args(case, conv)
         requests, width = case.slots.shape
-        tokens = case.tokens
         hv, h = case.num_v_heads, case.num_k_heads
         dim = case.qkv.shape[1]
         conv_width = conv.weight.shape[1]
         # Per token, besides the decode's bytes: the conv reads the window ((width - 1) bf16
         # positions of every channel) and the pre-conv row, writes the shifted state
         # (width - 2 + 1 positions) and the post-conv row.
-        conv_bytes = tokens * dim * 2 * ((conv_width - 1) + (conv_width - 1) + 2)
-        bytes_per_launch = workloads.decode_algorithmic_bytes(requests, width, tokens, h, hv) + conv_bytes
-        touched = requests * 2 * hv * workloads.SLOT_HEAD_BYTES
+        conv_bytes = case.tokens * dim * 2 * ((conv_width - 1) + (conv_width - 1) + 2)
 
         def fn():
             torch.ops.lightdelta.conv_decode(*fused_args)
 
-        units_per_step, unit = tokens, "tokens/s"
         config = {"workload": "config2_conv_decode", "sequences_per_gpu": requests, "tokens_per_sequence": width,
                   "num_k_heads": h, "num_v_heads": hv, "conv_width": conv_width, "conv_state_dtype": "bf16",
                   "conv_layout": "[slots, dim, L]", "launches_per_step": "conv update + decode",
                   "vllm_pipeline": unfused_conv_decode_us(case, conv, stream)}
-        case = None
-    elif args.workload == "sample":
+        # The two kernels (conv update, decode) are accounted together as one step.
+        return Workload(fn, workloads.decode_algorithmic_bytes(requests, width, case.tokens, h, hv) + conv_bytes,
+                        requests * 2 * hv * workloads.SLOT_HEAD_BYTES, case.tokens, "tokens/s", config,
+                        kernels_per_step=2)
+    if name == "sample":
         sampling = workloads.sampling_case(device, seed=6 + seed)
         turn = [0]
 
@@ -333,15 +334,15 @@ def run_ours(args, dist: Dist) -> dict | None:
             turn[0] += 1
             torch.ops.lightdelta.greedy_verify(*sampling.op_args(buffer))
 
-        bytes_per_launch = sampling.bytes_per_launch()
-        touched = bytes_per_launch * len(sampling.logits)
-        units_per_step, unit = sampling.requests, "requests/s"
-        case = None
         rows, vocab = sampling.logits[0].shape
         config = {"workload": "config3_greedy_verify", "requests_per_gpu": sampling.requests,
                   "draft_tokens": sampling.sampled.shape[1] - 1, "logits_rows": rows, "vocab": vocab,
                   "logits_dtype": "fp32", "logits_buffers_in_turn": len(sampling.logits)}
-    elif args.workload == "stacked":
+        w = Workload(fn, sampling.bytes_per_launch(), sampling.bytes_per_launch() * len(sampling.logits),
+                     sampling.requests, "requests/s", config, dtype="fp32 logits, int32 tokens")
+        w.sampling = sampling
+        return w
+    if name == "stacked":
         from lightdelta_b200 import sharding
 
         total_sequences, layers, width = 2048, 48, 4
@@ -366,16 +367,14 @@ def run_ours(args, dist: Dist) -> dict | None:
         def fn():
             graph.replay()
 
-        bytes_per_launch = wl.step_bytes() // layers
-        touched = wl.step_bytes()
-        units_per_step, unit = local * width, "tokens/s"
-        case = None
         config = {"workload": "config5_stacked_verify", "layers": layers, "sequences_total": total_sequences,
                   "sequences_per_gpu": local, "tokens_per_sequence": width, "num_k_heads": 16, "num_v_heads": 32,
                   "physical_layer_pools": len(wl.pools),
                   "pool_slots_per_layer": wl.pools[0].shape[0], "cuda_graph": "one graph of 48 decode launches",
                   "decode_kernel": args.decode_kernel}
-    else:
+        return Workload(fn, wl.step_bytes() // layers, wl.step_bytes(), local * width, "tokens/s", config,
+                        launches_per_step=layers, cleanup=graph.reset)
+    if name == "copy":
         pool = torch.empty(2048, 32, 128, 128, device=device)
         pool.normal_(0.0, 0.02)
         gather_idx, scatter_idx = workloads.config4_indices(device, seed=4 + seed)
@@ -387,23 +386,45 @@ def run_ours(args, dist: Dist) -> dict | None:
             torch.ops.lightdelta.scatter_state(packed, scatter_idx, pool)
 
         bytes_per_launch = 512 * 32 * workloads.SLOT_HEAD_BYTES * 2  # per op: read + write 512 slots
-        touched = bytes_per_launch * 2
-        units_per_step, unit = 512, "slots/s"
         config = {"workload": "config4_copy", "pool_slots": 2048, "slots_per_step": 512,
                   "ops_per_step": ["gather_state", "scatter_state"], "num_v_heads": 32, "head_dim": 128}
+        return Workload(fn, bytes_per_launch, bytes_per_launch * 2, 512, "slots/s", config, launches_per_step=2,
+                        dtype="fp32 (bit copy)")
+    raise ValueError(name)
 
-    total_ms, launch_ms, window = timed_launches(fn, args.steps, args.warmup, dist, stream)
-    sampler.mark(*window)
-    clocks = sampler.summary()
+
+# Secondary results of the default (config 2) line: BASELINE configs 3 and 4 and the bf16 pool.
+EXTRA_WORKLOADS = ("verify", "copy", "decode_bf16", "verify_bf16")
+
+
+def measure(w: Workload, steps: int, warmup: int, dist: Dist, stream, peaks: dict) -> dict:
+    total_ms, launch_ms, window = timed_launches(w.fn, steps, warmup, dist, stream)
     max_ms = dist.max(total_ms)
-    # Equal-size launches of the dominant kernel per step (the roofline's unit); the conv workload's
-    # two kernels (conv update, decode) are accounted together as one step.
-    launches_per_step = {"copy": 2, "stacked": 48}.get(args.workload, 1)
-    kernels_per_step = {"conv": 2}.get(args.workload, launches_per_step)
-    kernel_ms = launch_ms / launches_per_step
-    achieved_gbs = bytes_per_launch / (kernel_ms * 1e-3) / 1e9
-    value = dist.sum(units_per_step) * args.steps / (max_ms * 1e-3)
-    state_gbs_total = dist.sum(bytes_per_launch * launches_per_step * args.steps / (total_ms * 1e-3) / 1e9)
+    kernel_ms = launch_ms / w.launches_per_step
+    achieved = w.bytes_per_launch / (kernel_ms * 1e-3) / 1e9
+    return {"total_ms": total_ms, "max_ms": max_ms, "kernel_ms": kernel_ms, "achieved_gbs": achieved,
+            "frac": achieved / peaks["hbm_gbs"], "window": window,
+            "value": dist.sum(w.units_per_step) * steps / (max_ms * 1e-3),
+            "state_gbs": dist.sum(w.bytes_per_launch * w.launches_per_step * steps / (total_ms * 1e-3) / 1e9)}
+
+
+def run_ours(args, dist: Dist) -> dict | None:
+    import torch
+
+    from lightdelta_b200 import capi, ops  # noqa: F401
+
+    capi.set_decode_kernel(args.decode_kernel)
+    torch.cuda.set_device(dist.local_rank)
+    device = torch.device("cuda", dist.local_rank)
+    stream = torch.cuda.current_stream(device)
+    sampler = ClockSampler(device.index if device.index is not None else 0)
+    peaks = measured_peaks()
+
+    w = build_workload(args.workload, args, dist, device, stream)
+    m = measure(w, args.steps, args.warmup, dist, stream, peaks)
+    sampler.mark(*m["window"])
+    clocks = sampler.summary()
+    case = w.case
 
     e2e = None
     if args.workload in ("decode", "verify"):
@@ -412,47 +433,70 @@ def run_ours(args, dist: Dist) -> dict | None:
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline and args.workload in ("decode", "verify"):
         cpu = cpu_baseline(case, args.cpu_seconds)
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline and args.workload == "sample":
-        cpu = sampling_cpu_baseline(sampling, args.cpu_seconds)
+        cpu = sampling_cpu_baseline(w.sampling, args.cpu_seconds)
+    if w.cleanup is not None:
+        w.cleanup()
+
+    main = {"unit": w.unit, "config": w.config, "dtype": w.dtype, "touched": w.touched,
+            "bytes_per_launch": w.bytes_per_launch, "kernels_per_step": w.kernels_per_step}
+    extra = None
+    if args.workload == "decode" and not args.no_extras:
+        del w, case
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        extra = {}
+        for name in EXTRA_WORKLOADS:
+            xw = build_workload(name, args, dist, device, stream)
+            steps = max(args.steps, 50)
+            xm = measure(xw, steps, args.warmup, dist, stream, peaks)
+            extra[name] = {"workload": xw.config["workload"], "value": xm["value"], "unit": xw.unit,
+                           "ms_per_launch": xm["kernel_ms"], "launches_per_step": xw.launches_per_step,
+                           "algorithmic_bytes_per_launch": xw.bytes_per_launch, "achieved_gbs": xm["achieved_gbs"],
+                           "frac": xm["frac"], "peak_gbs": peaks["hbm_gbs"], "dtype": xw.dtype, "steps": steps,
+                           "traffic": ncu_traffic(name)}
+            del xw
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
 
     if dist.rank != 0:
         return None
-    traffic = ncu_traffic(args.workload)
-    return {
+    result = {
         "metric": METRIC,
-        "value": value,
-        "unit": unit,
+        "value": m["value"],
+        "unit": main["unit"],
         "n_gpus": dist.world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": max_ms / args.steps,
+        "ms_per_step": m["max_ms"] / args.steps,
         "higher_is_better": True,
         "scaling": "strong" if args.workload == "stacked" else "weak",
         "vs_baseline": None,
-        "dtype": {"copy": "fp32 (bit copy)", "commit": "fp32 (bit copy)",
-                  "sample": "fp32 logits, int32 tokens", "decode_bf16": "fp32 (bf16 state pool)",
-                  "verify_bf16": "fp32 (bf16 state pool)"}.get(args.workload, "fp32"),
+        "dtype": main["dtype"],
         "data": "synthetic (seeded, BASELINE config shapes and distributions)",
         "impl": "ours",
-        "config": {**config, "parallelism": f"slot-sharded x{dist.world}, no collective",
-                   "l2": f"no flush: the {touched / 1e9:.2f} GB touched per step exceeds the 126 MB L2"},
-        "state_gbs": state_gbs_total,
-        "hbm_frac_of_8tbs_per_gpu": state_gbs_total / dist.world / NOMINAL_HBM_GBS,
+        "config": {**main["config"], "parallelism": f"slot-sharded x{dist.world}, no collective",
+                   "l2": f"no flush: the {main['touched'] / 1e9:.2f} GB touched per step exceeds the 126 MB L2"},
+        "state_gbs": m["state_gbs"],
+        "hbm_frac_of_8tbs_per_gpu": m["state_gbs"] / dist.world / NOMINAL_HBM_GBS,
         "roofline": {
             "bound": "hbm",
-            "achieved": achieved_gbs,
+            "achieved": m["achieved_gbs"],
             "peak": peaks["hbm_gbs"],
             "unit": "GB/s",
-            "frac": achieved_gbs / peaks["hbm_gbs"],
+            "frac": m["frac"],
             "peak_source": peaks["source"],
-            "traffic": traffic,
-            "algorithmic_bytes_per_launch": bytes_per_launch,
-            "kernel_ms": kernel_ms,
+            "traffic": ncu_traffic(args.workload),
+            "algorithmic_bytes_per_launch": main["bytes_per_launch"],
+            "kernel_ms": m["kernel_ms"],
         },
         "e2e": e2e,
         "cpu_baseline": cpu,
-        "gpu_launches": kernels_per_step * args.steps,
+        "gpu_launches": main["kernels_per_step"] * args.steps,
         "clocks": clocks,
     }
+    if extra is not None:
+        result["extra"] = extra
+    return result
 
 
 def gpu_local_cpus(device_index: int):
@@ -479,7 +523,9 @@ def gpu_local_cpus(device_index: int):
 def run_e2e(case, args, dist: Dist, stream) -> dict:
     """Same metric through the public op with host buffers.  Every step copies its activations
     and request metadata from pinned host memory, runs torch.ops.lightdelta.decode and reads the
-    output back to pinned host memory.  Two buffer sets let the copies of one step overlap the
+    output back to pinned host memory.  A step's inputs (the projection rows, the a/b rows, slots,
+    cu and accepted counts) sit in one pinned staging buffer, so one copy carries them; the op
+    reads views of the device copy.  Two buffer sets let the copies of one step overlap the
     kernel of the neighbouring step (H2D, compute and D2H on three streams); the state pool is
     shared, so the kernels still run strictly in order."""
     import torch
@@ -492,20 +538,35 @@ def run_e2e(case, args, dist: Dist, stream) -> dict:
     try:
         proj = case.qkv.as_strided((case.tokens, case.qkv.stride(0)), (case.qkv.stride(0), 1))
         ba = case.b.as_strided((case.tokens, case.b.stride(0)), (case.b.stride(0), 1))
+        parts = [("proj", proj), ("ba", ba), ("slots", case.slots), ("cu", case.cu), ("accepted", case.accepted)]
+        offsets, size = {}, 0
+        for name, t in parts:
+            offsets[name] = size
+            size += -(-t.numel() * t.element_size() // 256) * 256  # 256-byte aligned sections
         qkv_width, hv = case.qkv.shape[1], case.num_v_heads
-        names = ("proj", "ba", "slots", "cu", "accepted")
-        host = [{n: t.cpu().pin_memory() for n, t in zip(names, (proj, ba, case.slots, case.cu, case.accepted))}
-                for _ in range(2)]
+
+        def views(buf):
+            out = {}
+            for name, t in parts:
+                nbytes = t.numel() * t.element_size()
+                out[name] = buf[offsets[name]:offsets[name] + nbytes].view(t.dtype).view(t.shape)
+            return out
+
+        host = [torch.empty(size, dtype=torch.uint8).pin_memory() for _ in range(2)]
+        for b in range(2):
+            hv_views = views(host[b])
+            for name, t in parts:
+                hv_views[name].copy_(t.cpu())
+        dev = [torch.empty(size, dtype=torch.uint8, device=device) for _ in range(2)]
         out_h = [torch.empty(case.out.shape, dtype=case.out.dtype).pin_memory() for _ in range(2)]
-        dev = [{n: torch.empty_like(t, device=device) for n, t in host[0].items()} for _ in range(2)]
         out_d = [torch.empty_like(case.out) for _ in range(2)]
         args_of = []
         for b in range(2):
-            d = dev[b]
+            d = views(dev[b])
             args_of.append((d["proj"][:, :qkv_width], d["ba"][:, hv:], d["ba"][:, :hv], case.a_log, case.dt_bias,
                             d["slots"], d["cu"], d["accepted"], case.pool,
                             d["proj"][:, qkv_width:].view(case.tokens, hv, 128), case.weight, out_d[b], case.eps))
-        h2d = sum(t.numel() * t.element_size() for t in host[0].values())
+        h2d = size
         d2h = out_h[0].numel() * out_h[0].element_size()
         s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
         ev_h2d = [torch.cuda.Event() for _ in range(2)]
@@ -514,24 +575,24 @@ def run_e2e(case, args, dist: Dist, stream) -> dict:
         for b in range(2):
             ev_kernel[b].record(stream)
             ev_d2h[b].record(stream)
+        decode = torch.ops.lightdelta.decode
 
         def step(i: int):
             b = i & 1
+            s_in.wait_event(ev_kernel[b])              # step i-2 has finished reading dev[b]
             with torch.cuda.stream(s_in):
-                s_in.wait_event(ev_kernel[b])          # step i-2 has finished reading dev[b]
-                for n in names:
-                    dev[b][n].copy_(host[b][n], non_blocking=True)
-                ev_h2d[b].record(s_in)
+                dev[b].copy_(host[b], non_blocking=True)
+            ev_h2d[b].record(s_in)
             stream.wait_event(ev_h2d[b])
             stream.wait_event(ev_d2h[b])               # step i-2's output has been read back
-            torch.ops.lightdelta.decode(*args_of[b])
+            decode(*args_of[b])
             ev_kernel[b].record(stream)
+            s_out.wait_event(ev_kernel[b])
             with torch.cuda.stream(s_out):
-                s_out.wait_event(ev_kernel[b])
                 out_h[b].copy_(out_d[b], non_blocking=True)
-                ev_d2h[b].record(s_out)
+            ev_d2h[b].record(s_out)
 
-        steps = min(args.e2e_steps, args.steps)
+        steps = args.e2e_steps
         for i in range(args.warmup):
             step(i)
         torch.cuda.synchronize()
@@ -539,8 +600,10 @@ def run_e2e(case, args, dist: Dist, stream) -> dict:
         begin, finish = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         begin.record(stream)
         s_in.wait_stream(stream)
+        host0 = time.perf_counter()
         for i in range(steps):
             step(i)
+        host_us = (time.perf_counter() - host0) * 1e6 / steps
         stream.wait_stream(s_out)
         finish.record(stream)
         torch.cuda.synchronize()
@@ -550,8 +613,9 @@ def run_e2e(case, args, dist: Dist, stream) -> dict:
         os.sched_setaffinity(0, saved_affinity)
     return {"value": case.tokens * steps * dist.world / (max_ms * 1e-3), "unit": "tokens/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
-            "api": "torch.ops.lightdelta.decode, pinned host buffers, double-buffered H2D/D2H overlapping the "
-                   "neighbouring step's kernel",
+            "ms_per_step": max_ms / steps, "host_enqueue_us_per_step": host_us,
+            "api": "torch.ops.lightdelta.decode; inputs from one pinned staging buffer per step (one H2D copy), "
+                   "output to pinned memory; double-buffered so copies overlap the neighbouring step's kernel",
             "host_cpus": len(local) if local else None}
 
 
@@ -685,6 +749,55 @@ def sampling_cpu_baseline(sampling, seconds: float) -> dict:
                       f"{elapsed:.1f} s, C oracle (argmax + prefix check) with OpenMP"}
 
 
+def reference_gpu_kernel(steps: int, warmup: int) -> dict:
+    """The reference's own CUDA kernel (oracle/_ref/libref_harness.so: csrc/gdn_decode.cu compiled
+    unmodified, its kernel template launched at value-head ratio 2 = the BASELINE geometry) on
+    configs 2 and 3, timed like our arm: back-to-back in-place launches on a pool larger than L2,
+    one CUDA event pair over the timed launches."""
+    import torch
+
+    from lightdelta_b200 import workloads
+    from oracle import ref_kernel
+
+    if not torch.cuda.is_available():
+        return {"unavailable": "no GPU visible"}
+    if not ref_kernel.available():
+        return {"unavailable": "oracle/_ref/libref_harness.so not built (python oracle/build_ref.py)"}
+    device = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream(device)
+    peak = measured_peaks()["hbm_gbs"]
+    result = {"kernel": "gdn_decode_post_conv_mtp_kernel<float, 2, false> (csrc/gdn_decode.cu:130-354), "
+                        "grid (requests, HV) x 256 threads as the stock launcher (csrc/gdn_decode.cu:407-418)",
+              "peak_gbs": peak}
+    for name, builder in (("config2_decode", workloads.config2), ("config3_verify", workloads.config3)):
+        case = builder(device)
+        op_args = case.op_args()
+        requests, width = case.slots.shape
+
+        def fn():
+            ref_kernel.decode(*op_args)
+
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        begin, finish = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        count = max(steps, 50)
+        begin.record(stream)
+        for _ in range(count):
+            fn()
+        finish.record(stream)
+        torch.cuda.synchronize()
+        us = begin.elapsed_time(finish) * 1000 / count
+        algorithmic = workloads.decode_algorithmic_bytes(requests, width, case.tokens, case.num_k_heads,
+                                                         case.num_v_heads)
+        achieved = algorithmic / (us * 1e-6) / 1e9
+        result[name] = {"us_per_launch": us, "tokens_per_s": case.tokens / (us * 1e-6), "achieved_gbs": achieved,
+                        "frac": achieved / peak, "launches": count}
+        del case, op_args
+        torch.cuda.empty_cache()
+    return result
+
+
 def run_reference(args, dist: Dist) -> dict | None:
     if dist.rank != 0:
         return None
@@ -740,6 +853,7 @@ def run_reference(args, dist: Dist) -> dict | None:
                    "parallelism": "rank 0 host CPU only"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "reference_gpu_kernel": reference_gpu_kernel(args.steps, args.warmup),
     }
 
 

@@ -7,6 +7,12 @@ must be loaded in a process of its own.  The GPU tests use it as a second, indep
 (the reference kernel itself at its HV=48 geometry) and as the kernel to compare against.
 Nothing is copied from the reference tree; nothing is written outside oracle/_ref/.
 
+It also builds oracle/_ref/libref_harness.so from oracle/ref_geometry_harness.cu, which includes
+the reference's csrc/gdn_decode.cu unmodified and launches its kernel template at value-head ratio
+2 or 3 through one C function (the stock launcher only runs ratio 3, HV=48), so the reference
+kernel can run at the BASELINE geometry (H=16, HV=32).  It registers no torch operators, so it
+can share a process with lightdelta_b200.
+
 Run here (where the reference sources exist):  python oracle/build_ref.py [--reference DIR]
 """
 
@@ -70,11 +76,36 @@ def build(reference: Path = DEFAULT_REFERENCE, force: bool = False) -> Path:
     return OUT
 
 
+HARNESS_SRC = HERE / "ref_geometry_harness.cu"
+HARNESS = OUT_DIR / "libref_harness.so"
+
+
+def build_harness(reference: Path = DEFAULT_REFERENCE, force: bool = False) -> Path:
+    kernel = reference / "csrc" / "gdn_decode.cu"
+    if not kernel.exists():
+        raise FileNotFoundError(f"reference kernel not found: {kernel}")
+    deps = [kernel, HARNESS_SRC, reference / "include" / "lightdelta" / "ops.h"]
+    if HARNESS.exists() and not force and all(d.stat().st_mtime <= HARNESS.stat().st_mtime for d in deps):
+        return HARNESS
+    OUT_DIR.mkdir(parents=True, exist_ok=True)
+    includes, lib, abi = _torch_flags()
+    tmp = HARNESS.with_suffix(".tmp.so")
+    cmd = ["/usr/local/cuda/bin/nvcc", "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17",
+           "--expt-relaxed-constexpr", "-lineinfo", "-shared", "-Xcompiler", "-fPIC",
+           f"-D_GLIBCXX_USE_CXX11_ABI={abi}", *[f"-I{p}" for p in includes], f"-I{reference}",
+           f"-I{reference / 'include'}", str(HARNESS_SRC), "-o", str(tmp), f"-L{lib}", "-lc10", "-lc10_cuda",
+           "-ltorch_cpu", "-ltorch", f"-Xlinker=-rpath,{lib}"]
+    subprocess.run(cmd, check=True)
+    os.replace(tmp, HARNESS)
+    return HARNESS
+
+
 def build_if_available() -> Path | None:
     """Builds oracle/_ref/_C.so when the reference sources are present (this container); on the
     GPU box the prebuilt library is used as shipped."""
     if not DEFAULT_REFERENCE.exists():
         return OUT if OUT.exists() else None
+    build_harness(DEFAULT_REFERENCE)
     return build(DEFAULT_REFERENCE)
 
 
@@ -84,6 +115,7 @@ def main() -> int:
     parser.add_argument("--force", action="store_true")
     args = parser.parse_args()
     print(build(args.reference, args.force))
+    print(build_harness(args.reference, args.force))
     return 0
 
 

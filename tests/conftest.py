@@ -36,3 +36,24 @@ def device(native):
     from lightdelta_b200 import ops  # noqa: F401
 
     return torch.device("cuda", 0)
+
+
+def pytest_terminal_summary(terminalreporter):
+    """Largest measured outlier rate of each kind of tolerance check run in this session."""
+    try:
+        from helpers import MEASURED
+    except ImportError:
+        return
+    if not MEASURED:
+        return
+    worst = {}
+    for kind, what, count, size, ulps in MEASURED:
+        rate = count / size if size else 0.0
+        best = worst.get(kind)
+        if best is None or rate > best[0]:
+            worst[kind] = (rate, count, size, what, max(ulps, best[4] if best else 0))
+        else:
+            worst[kind] = best[:4] + (max(ulps, best[4]),)
+    terminalreporter.write_line("tolerance checks, largest outlier rate per kind (rate, count, elements, where, max ulps):")
+    for kind, (rate, count, size, what, ulps) in sorted(worst.items()):
+        terminalreporter.write_line(f"  {kind}: {rate:.2e} ({count} of {size}) at '{what}', max {ulps} ulps overall")

@@ -21,6 +21,10 @@ NORTH_ATOL, NORTH_RTOL = 2e-3, 2e-3
 OUT_REF_ATOL, OUT_REF_RTOL = 0.008, 0.02
 MAX_FLIP_FRACTION = 1e-3
 
+# Measured outlier rates of every tolerance check in this session (printed at the end of the run
+# by tests/conftest.py), so the bounds above can be kept close to what the kernels achieve.
+MEASURED: list = []
+
 
 def bits(t: torch.Tensor) -> np.ndarray:
     """Raw bf16 bits of a tensor as a numpy uint16 array (copied to the host)."""
@@ -40,7 +44,8 @@ def bf16_ulp_distance(a_bits: np.ndarray, b_bits: np.ndarray) -> np.ndarray:
     return np.abs(_ordinal(a_bits) - _ordinal(b_bits))
 
 
-def assert_out_close(actual_bits: np.ndarray, expected_bits: np.ndarray, what: str = "out") -> dict:
+def assert_out_close(actual_bits: np.ndarray, expected_bits: np.ndarray, what: str = "out",
+                     max_outlier_ulps: int = 1, max_fraction: float = MAX_FLIP_FRACTION) -> dict:
     actual = bf16_values(actual_bits).astype(np.float64)
     expected = bf16_values(expected_bits).astype(np.float64)
     assert actual.shape == expected.shape, f"{what}: shape {actual.shape} != {expected.shape}"
@@ -50,11 +55,14 @@ def assert_out_close(actual_bits: np.ndarray, expected_bits: np.ndarray, what: s
     north_ok = diff <= NORTH_ATOL + NORTH_RTOL * np.abs(expected)
     ulps = bf16_ulp_distance(actual_bits, expected_bits)
     outliers = ~north_ok
-    assert (ulps[outliers] <= 1).all(), f"{what}: an element outside 2e-3 differs by more than one bf16 ulp"
+    worst = int(ulps[outliers].max()) if outliers.any() else 0
+    assert worst <= max_outlier_ulps, (f"{what}: an element outside 2e-3 differs by {worst} bf16 ulps "
+                                       f"({int(outliers.sum())} outside 2e-3)")
     fraction = outliers.mean() if outliers.size else 0.0
-    assert fraction <= MAX_FLIP_FRACTION, f"{what}: {outliers.sum()} one-ulp flips ({fraction:.2e} of elements)"
+    MEASURED.append(("out", what, int(outliers.sum()), int(outliers.size), worst))
+    assert fraction <= max_fraction, f"{what}: {outliers.sum()} rounding flips ({fraction:.2e} of elements)"
     return dict(elements=int(actual.size), exact=int((ulps == 0).sum()), one_ulp=int((ulps == 1).sum()),
-                outside_2e3=int(outliers.sum()), max_diff=float(diff.max()) if diff.size else 0.0)
+                outside_2e3=int(outliers.sum()), outlier_ulps=worst, max_diff=float(diff.max()) if diff.size else 0.0)
 
 
 # A bf16 state pool: the device and the oracle both run the recurrence in fp32 and round each
@@ -82,6 +90,7 @@ def assert_bf16_state_close(actual_bits: np.ndarray, expected_bits: np.ndarray, 
         raise AssertionError(f"{what}: {int((~ok).sum())} elements more than {max_ulps} bf16 ulps and "
                              f"3e-6 / 3e-4 apart (actual, expected): {worst}")
     fraction = float((ulps >= 1).mean()) if ulps.size else 0.0
+    MEASURED.append(("bf16 state", what, int((ulps >= 1).sum()), int(ulps.size), int(ulps.max()) if ulps.size else 0))
     assert fraction <= BF16_STATE_MAX_FLIP_FRACTION, f"{what}: {int((ulps >= 1).sum())} differ ({fraction:.2e})"
     return dict(elements=int(ulps.size), one_ulp=int((ulps == 1).sum()), more=int((ulps > 1).sum()),
                 max_diff=float(diff.max()) if diff.size else 0.0)
@@ -125,6 +134,9 @@ def assert_out_close_tail(actual_bits: np.ndarray, expected_bits: np.ndarray, wh
     assert ref_ok.all(), f"{what}: {int((~ref_ok).sum())} elements outside atol 0.008 / rtol 0.02, max diff {diff.max()}"
     outliers = diff > NORTH_ATOL + NORTH_RTOL * np.abs(expected)
     fraction = float(outliers.mean()) if outliers.size else 0.0
+    ulps = bf16_ulp_distance(actual_bits, expected_bits)
+    MEASURED.append(("out tail", what, int(outliers.sum()), int(outliers.size),
+                     int(ulps[outliers].max()) if outliers.any() else 0))
     assert fraction <= MAX_FLIP_FRACTION, f"{what}: {outliers.sum()} elements outside 2e-3 ({fraction:.2e})"
     return dict(outside_2e3=int(outliers.sum()), max_diff=float(diff.max()) if diff.size else 0.0)
 

@@ -369,8 +369,18 @@ int prepare_conv(void* x, int64_t x_row_stride, int64_t n_tokens, int64_t dim, v
   if (n_requests < 0 || n_tokens < 0 || dim < 1 || n_requests > 65535) {
     return set_error(LD_ERR_INVALID, "conv: need 0 <= requests <= 65535, tokens >= 0 and dim >= 1");
   }
-  if (x_row_stride < dim || n_conv_slots < 1 || conv_slot_stride < 0 || conv_dim_stride < 1 || conv_pos_stride < 1) {
+  if (x_row_stride < dim || n_conv_slots < 1 || conv_slot_stride < 0 || conv_dim_stride < 1 || conv_pos_stride < 1 ||
+      slots_stride < 1) {
     return set_error(LD_ERR_INVALID, "conv: invalid strides or slot count");
+  }
+  // Each request updates its window in place, so two (slot, channel, position) triples must never
+  // share an element: channel and position strides must not overlap inside a slot, and slots must
+  // not overlap each other.
+  const bool dims_disjoint =
+      conv_dim_stride >= conv_state_len * conv_pos_stride || conv_pos_stride >= dim * conv_dim_stride;
+  const int64_t slot_extent = (dim - 1) * conv_dim_stride + (conv_state_len - 1) * conv_pos_stride + 1;
+  if (!dims_disjoint || (n_conv_slots > 1 && conv_slot_stride < slot_extent)) {
+    return set_error(LD_ERR_INVALID, "conv: the conv state's strides make slots, channels or positions overlap");
   }
   if (n_requests > 0 && (x == nullptr || conv_state == nullptr || conv_weight == nullptr || slots == nullptr ||
                          cu == nullptr)) {

@@ -158,10 +158,14 @@ class StackedWorkload:
 
 def stacked_workload(device, sequences: int, layers: int = 48, width: int = 4, seed: int = 5,
                      max_pool_bytes: int | None = None, num_k_heads: int = 16,
-                     num_v_heads: int = 32) -> StackedWorkload:
-    """Config 5: `sequences` local sequences, `width`-token MTP verify, `layers` layers."""
+                     num_v_heads: int = 32, pool_slots: int | None = None) -> StackedWorkload:
+    """Config 5: `sequences` local sequences, `width`-token MTP verify, `layers` layers.
+    Each physical pool has `pool_slots` slots (default: the null slot plus one per (sequence, step))."""
     slot_bytes = num_v_heads * SLOT_HEAD_BYTES
-    pool_slots = 1 + sequences * width
+    if pool_slots is None:
+        pool_slots = 1 + sequences * width
+    if pool_slots < 1 + sequences * width:
+        raise ValueError("pool_slots must hold the null slot and one slot per (sequence, step)")
     pool_bytes = pool_slots * slot_bytes
     physical = layers
     if max_pool_bytes is not None:

@@ -30,6 +30,20 @@ def make(device, batch, width, *, heads=(16, 32), layout="dim_first", seed=5, bi
     return case, conv
 
 
+def make_ragged(case, seed):
+    """Mixed 1..width tokens per request (vLLM's varlen path: each request's conv state length shrinks
+    by the tokens it lacks); the unowned tail rows of qkv stay as they are."""
+    batch, width = case.slots.shape
+    gen = torch.Generator().manual_seed(seed)
+    lengths = torch.randint(1, width + 1, (batch,), generator=gen, dtype=torch.int32)
+    lengths[0] = width
+    lengths[1] = 1
+    cu = torch.zeros(batch + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(lengths, 0)
+    case.cu.copy_(cu.to(case.cu.device))
+    return case
+
+
 def oracle_fused(case, conv):
     """Host copies -> oracle conv update -> oracle decode; returns (out bits, pool, conv storage,
     post-conv qkv bits)."""
@@ -132,11 +146,14 @@ def test_oracle_conv_matches_vllm_kernel_bf16(device, width):
     assert (diff != 0).mean() < 1e-3, f"{(diff != 0).mean():.2e} of post-conv values differ by one ulp"
 
 
-@pytest.mark.parametrize("width", [1, 4])
-def test_fused_equals_vllm_conv_then_decode(device, width):
-    """The fused op against the pipeline it replaces: vLLM's conv kernel, then lightdelta::decode."""
+@pytest.mark.parametrize("width, ragged", [(1, False), (4, False), (4, True)])
+def test_fused_equals_vllm_conv_then_decode(device, width, ragged):
+    """The fused op against the pipeline it replaces: vLLM's conv kernel, then lightdelta::decode;
+    with `ragged`, requests carry 1..4 tokens."""
     causal_conv1d_update = _vllm_conv()
     case, conv = make(device, 48, width, seed=41)
+    if ragged:
+        make_ragged(case, 42)
     unfused_pool, unfused_state = case.pool.clone(), conv.state.clone()
     x = case.qkv.clone()
     slots0 = case.slots[:, 0].contiguous()
@@ -147,7 +164,8 @@ def test_fused_equals_vllm_conv_then_decode(device, width):
         y = causal_conv1d_update(x, unfused_state, conv.weight, None, "silu", conv_state_indices=slots0,
                                  num_accepted_tokens=case.accepted, query_start_loc=case.cu, max_query_len=width,
                                  validate_data=False)
-    unfused_out = torch.empty_like(case.out)
+    unfused_out = torch.zeros_like(case.out)
+    case.out.zero_()  # rows no request owns (ragged case) stay zero in both
     torch.ops.lightdelta.decode(y, case.a, case.b, case.a_log, case.dt_bias, case.slots, case.cu, case.accepted,
                                 unfused_pool, case.gate, case.weight, unfused_out, 1e-6)
     torch.ops.lightdelta.conv_decode(*workloads.conv_decode_args(case, conv))
@@ -247,12 +265,14 @@ def test_conv_update_matches_oracle(device, layout, conv_width, spec):
     assert_post_conv_close(host_bf16(x), post)
 
 
-@pytest.mark.parametrize("width", [1, 4])
-def test_conv_update_equals_vllm_kernel(device, width):
+@pytest.mark.parametrize("width, ragged", [(1, False), (4, False), (4, True)])
+def test_conv_update_equals_vllm_kernel(device, width, ragged):
     """Our conv kernel against vLLM's on the same GPU: identical state, post-conv values equal
-    but for exp rounding."""
+    but for exp rounding; with `ragged`, requests carry 1..4 tokens."""
     causal_conv1d_update = _vllm_conv()
     case, conv = make(device, 64, width, seed=81)
+    if ragged:
+        make_ragged(case, 82)
     slots0 = case.slots[:, 0].contiguous()
     x_ref, state_ref = case.qkv.contiguous().clone(), conv.state.clone()
     if width == 1:

@@ -55,6 +55,10 @@ def test_bf16_products_are_rounded():
     ({1: 10}, "invalid strides"),        # x_row_stride < dim
     ({0: None}, "NULL"),                 # x
     ({0: 1 << 20 | 1}, "2-byte aligned"),
+    ({6: 100}, "overlap"),               # conv slots closer than one slot's extent
+    ({6: 0}, "overlap"),                 # every request on the same slot storage
+    ({7: 2}, "overlap"),                 # channels closer than the window length
+    ({14: 0}, "invalid strides"),        # slot vector stride 0
 ])
 def test_capi_conv_update_rejects_bad_arguments_before_touching_the_gpu(native, change, message):
     """Host-side checks only: the addresses are never dereferenced (each call fails validation)."""

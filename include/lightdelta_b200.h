@@ -160,8 +160,11 @@ int ld_copy_slots(float* pool, int64_t n_pool_slots, int64_t pool_slot_stride,
  * tokens exactly as ld_decode does, and every stored step is rounded to bf16 (nearest even).
  * Half the state bytes of an fp32 pool per token; results differ from the fp32 pool by that
  * rounding and, within fp32 rounding, by the order of the dot products' additions (each lane
- * owns eight consecutive bf16 columns).  The streaming and one-CTA-per-item kernels both run it
- * (ld_decode_kernel_override applies).  No counterpart in the reference, whose
+ * owns eight consecutive bf16 columns).  One-token launches run a streaming kernel of their own
+ * (two items in flight per CTA, state kept as packed bf16 words, q / k norms folded into the
+ * reductions, so results also differ from the fp32 pool's in the last fp32 bits); multi-token
+ * launches always run the one-CTA-per-item kernel (LD_DECODE_KERNEL_STREAM applies to one-token
+ * launches only).  No counterpart in the reference, whose
  * launcher requires an fp32 pool (csrc/gdn_decode.cu:375-377).
  */
 int ld_decode_bf16_state(const void* qkv, int64_t qkv_row_stride, const void* a, int64_t a_row_stride,

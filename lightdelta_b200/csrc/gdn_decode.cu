@@ -30,10 +30,11 @@
 // items per SM, and when the activation rows are not 16-byte aligned (TMA bulk copies need
 // 16-byte aligned sources).
 //
-// Both kernels also read and write a bf16 state pool (ld_decode_bf16_state): the tile is an fp32
-// tile, widened on load and rounded to bf16 on store, with each lane owning eight consecutive
-// columns per half row ({64h + 8j .. 64h + 8j + 7 : h = 0, 1}, see tile_col) so that its state
-// accesses stay 16 bytes wide.
+// A bf16 state pool (ld_decode_bf16_state) runs the one-CTA-per-item kernel on an fp32 tile widened
+// on load and rounded to bf16 on store, each lane owning eight consecutive columns per half row
+// ({64h + 8j .. 64h + 8j + 7 : h = 0, 1}, see tile_col) so that its state accesses stay 16 bytes
+// wide; its one-token launches use gdn_decode_b16_kernel (namespace b16 below), which keeps two
+// items in flight per CTA.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -1042,6 +1043,286 @@ __global__ void __maxnreg__(168) gdn_decode_stream_kernel(const DecodeArgs p) {
   }
 }
 
+// ------------------------------------------------------------------------------------------
+// One-token decode on a bf16 pool: two items in flight per CTA.
+//
+// With half the state bytes per item, the per-item work of the consumer warps (a dependent chain
+// of smem loads, two row reductions and the stores) is the bound rather than HBM, and a register
+// tile of 64 fp32 values per thread leaves room for only 8 consumer warps.  Here each thread keeps
+// its 4 x 16 state values packed as bf16 pairs (32 registers instead of 64) and widens them twice,
+// once for S k and once for the update, S q and the stores; the bf16 k and q rows stay packed too,
+// with their L2 norms folded into the reductions and the update (o = q_scale / |q| sum S' q,
+// pred = sum (decay S) k / |k|, S' = decay S + (beta (v - pred) / |k|) k).  That frees enough
+// registers for two groups of 8 consumer warps, each taking every other item of the CTA's ring, so
+// one group's reductions and stores overlap the other's.  The producer warp and the ring are those
+// of the streaming kernel (TMA bulk copies, producer-side q / k norms).
+// ------------------------------------------------------------------------------------------
+namespace b16 {
+
+constexpr int kGroups = 2;
+constexpr int kGroupWarps = 8;
+constexpr int kGroupThreads = kGroupWarps * 32;          // 256: one Tile<4> per group
+constexpr int kThreads = kGroups * kGroupThreads + 64;   // + producer warp + norm warp
+constexpr int kRows = 4;
+constexpr int kRowGroups = Tile<kRows>::kRowGroups;      // 32
+
+struct ActStage1 {
+  __nv_bfloat16 q[1][kDim];
+  __nv_bfloat16 k[1][kDim];
+  __nv_bfloat16 v[1][kDim];
+  __nv_bfloat16 z[1][kDim];
+  ItemInfo info;
+};
+
+// The producer's view (produce() / publish_norms()) plus per-group output buffers.  The producer
+// only issues copies (kProducerNorms is false: it never waits for data); a norm warp of its own
+// publishes each item's q / k norms as soon as the item lands (norm_loop).
+struct Smem {
+  using State = __nv_bfloat16;
+  static constexpr int kStateStages = 6;
+  static constexpr int kActStages = 8;
+  static constexpr bool kProducerNorms = false;
+  static constexpr int kNormLag = 1;
+  __nv_bfloat16 state[kStateStages][kHeadElems];
+  ActStage1 act[kActStages];
+  float out[kGroups][2][kDim];
+  unsigned long long full[kStateStages];
+  unsigned long long empty_state[kStateStages];
+  unsigned long long empty_act[kActStages];
+  unsigned long long ready[kActStages];
+  unsigned long long out_full[kGroups][2];
+  unsigned long long out_empty[kGroups][2];
+  int abort;
+};
+static_assert(sizeof(Smem) <= 227 * 1024, "the bf16 ring must fit one CTA's shared memory");
+
+// Widens bf16 pair word w into (lo, hi) fp32.
+__device__ __forceinline__ float2 widen2(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
+// The same, widened again at each use: volatile, so that the compiler neither hoists the widened
+// k and q words (reused by every row) out of the row loop nor keeps the decayed state of the first
+// pass alive into the second -- either would hold 32 or 64 more fp32 values in registers.
+__device__ __forceinline__ float2 widen2_each(uint32_t w) {
+  uint32_t lo, hi;
+  asm volatile("shl.b32 %0, %2, 16;\n\tand.b32 %1, %2, 0xffff0000;" : "=r"(lo), "=r"(hi) : "r"(w));
+  return make_float2(__uint_as_float(lo), __uint_as_float(hi));
+}
+
+// One thread's 16 columns of one state row, as bf16 pairs: loaded from the stage, widened for the
+// two row products, and replaced by the updated row rounded to bf16.
+struct RowWords {
+  uint4 w[2];
+
+  __device__ __forceinline__ void load(const __nv_bfloat16* row) {
+    w[0] = *reinterpret_cast<const uint4*>(row);
+    w[1] = *reinterpret_cast<const uint4*>(row + 64);
+  }
+
+  // Partial sum of (decay S) k over the thread's columns (k: the raw bf16 row).
+  __device__ __forceinline__ float decayed_dot(float2 decay2, const uint4 (&kr)[2]) const {
+    float2 acc_a = make_float2(0.0f, 0.0f), acc_b = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t sw[4] = {w[h].x, w[h].y, w[h].z, w[h].w};
+      const uint32_t kw[4] = {kr[h].x, kr[h].y, kr[h].z, kr[h].w};
+      acc_a = fma2(mul2(widen2(sw[0]), decay2), widen2_each(kw[0]), acc_a);
+      acc_b = fma2(mul2(widen2(sw[1]), decay2), widen2_each(kw[1]), acc_b);
+      acc_a = fma2(mul2(widen2(sw[2]), decay2), widen2_each(kw[2]), acc_a);
+      acc_b = fma2(mul2(widen2(sw[3]), decay2), widen2_each(kw[3]), acc_b);
+    }
+    return (acc_a.x + acc_a.y) + (acc_b.x + acc_b.y);
+  }
+
+  // S' = decay S + dk k (kept as bf16 pairs) and the partial sum of S' q.
+  __device__ __forceinline__ float update(float2 decay2, float dk, const uint4 (&kr)[2], const uint4 (&qr)[2]) {
+    const float2 dk2 = make_float2(dk, dk);
+    float2 acc_a = make_float2(0.0f, 0.0f), acc_b = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t sw[4] = {w[h].x, w[h].y, w[h].z, w[h].w};
+      const uint32_t kw[4] = {kr[h].x, kr[h].y, kr[h].z, kr[h].w};
+      const uint32_t qw[4] = {qr[h].x, qr[h].y, qr[h].z, qr[h].w};
+      uint32_t nw[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 upd = fma2(widen2_each(kw[e]), dk2, mul2(widen2_each(sw[e]), decay2));
+        if (e & 1) {
+          acc_b = fma2(upd, widen2_each(qw[e]), acc_b);
+        } else {
+          acc_a = fma2(upd, widen2_each(qw[e]), acc_a);
+        }
+        nw[e] = pack_bf16x2(upd.x, upd.y);
+      }
+      w[h] = make_uint4(nw[0], nw[1], nw[2], nw[3]);
+    }
+    return (acc_a.x + acc_a.y) + (acc_b.x + acc_b.y);
+  }
+
+  __device__ __forceinline__ void store(__nv_bfloat16* row) const {
+    *reinterpret_cast<uint4*>(row) = w[0];
+    *reinterpret_cast<uint4*>(row + 64) = w[1];
+  }
+};
+
+__device__ void consume(const DecodeArgs& p, Smem& sm, int group, int tid) {
+  constexpr int kStates = Smem::kStateStages;
+  constexpr int kActs = Smem::kActStages;
+  const int HV = p.num_v_heads;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;  // within the group
+  const int j = tid & (kLanesPerRow - 1);
+  const int g = tid / kLanesPerRow;
+  int runs = 0;
+  int k = group;
+  for (int64_t item = blockIdx.x + static_cast<int64_t>(group) * gridDim.x; item < p.total_items;
+       item += static_cast<int64_t>(kGroups) * gridDim.x, k += kGroups) {
+    const int s = k % kStates;
+    const int a = k % kActs;
+    if (!warp_wait(&sm.full[s], (k / kStates) & 1, p.wait_ns) || !warp_wait(&sm.ready[a], (k / kActs) & 1, p.wait_ns)) {
+      if (lane == 0) set_abort(sm);
+      break;
+    }
+    const ItemInfo& info = sm.act[a].info;
+    const int kind = info.kind;
+    const int64_t bos = info.bos;
+    const int head = static_cast<int>(item % HV);
+    if (kind != kRun) {
+      if (kind == kZero) {
+        for (int idx = tid; idx < info.n * kDim; idx += kGroupThreads) {
+          const int64_t token = bos + idx / kDim;
+          p.out[(token * HV + head) * kDim + (idx % kDim)] = __float2bfloat16_rn(0.0f);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&sm.empty_state[s]);
+        mbar_arrive(&sm.empty_act[a]);
+      }
+      continue;
+    }
+    const ActStage1& act = sm.act[a];
+    uint4 kr[2], qr[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      kr[h] = *reinterpret_cast<const uint4*>(&act.k[0][64 * h + 8 * j]);
+      qr[h] = *reinterpret_cast<const uint4*>(&act.q[0][64 * h + 8 * j]);
+    }
+    const float decay = info.decay[0], beta = info.beta[0];
+    const float k_inv = info.k_inv[0], q_inv = info.q_inv[0];
+    const float2 decay2 = make_float2(decay, decay);
+    // This thread's rows g + 32 i, columns {64 h + 8 j .. + 7}, of the staged head and of the
+    // destination head, one row at a time from its stage words to its stored words, starting at row
+    // set blockIdx.x mod 4 (see store_tile).  Only 8 state words are live at a time: the 16 warps of
+    // the two groups hide each other's latencies instead of a 64-value tile per thread.
+    const __nv_bfloat16* srow = sm.state[s] + g * kDim + 8 * j;
+    const int dst = info.dst[0];
+    __nv_bfloat16* out_rows = dst > 0 ? state_base<__nv_bfloat16>(p) + static_cast<int64_t>(dst) * p.slot_stride +
+                                            static_cast<int64_t>(head) * kHeadElems + g * kDim + 8 * j
+                                      : nullptr;
+    const int buf = runs & 1;
+    const int use = runs >> 1;
+    if (use > 0 && !warp_wait(&sm.out_empty[group][buf], (use - 1) & 1, p.wait_ns)) {
+      if (lane == 0) set_abort(sm);
+      break;
+    }
+    float* o_buf = sm.out[group][buf];
+    const int first = blockIdx.x % kRows;
+#pragma unroll 1
+    for (int step = 0; step < kRows; ++step) {
+      const int i = (first + step) % kRows;
+      RowWords row;
+      row.load(srow + i * kRowGroups * kDim);
+      const float pred = row_sum(row.decayed_dot(decay2, kr)) * k_inv;
+      const float v = __bfloat162float(act.v[0][g + i * kRowGroups]);
+      // beta (v - pred) / |k|: the delta with k's norm folded in.
+      const float o = row_sum(row.update(decay2, (v - pred) * beta * k_inv, kr, qr)) * q_inv;
+      if (out_rows != nullptr) row.store(out_rows + i * kRowGroups * kDim);
+      if (j == 0) o_buf[g + i * kRowGroups] = __bfloat162float(__float2bfloat16_rn(o));
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.empty_state[s]);  // this warp's reads of the stage are done
+    // The gated RMSNorm of the item's token runs on one warp of the group, rotating from item to item.
+    const bool epilogue = warp == runs % kGroupWarps;
+    float z[4] = {0.f, 0.f, 0.f, 0.f};
+    float w[4] = {0.f, 0.f, 0.f, 0.f};
+    if (epilogue) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) w[e] = load_param(p.weight, 4 * lane + e, p.weight_bf16);
+      const uint2 raw = *reinterpret_cast<const uint2*>(&act.z[0][4 * lane]);
+      z[0] = bf16_lo(raw.x);
+      z[1] = bf16_hi(raw.x);
+      z[2] = bf16_lo(raw.y);
+      z[3] = bf16_hi(raw.y);
+    }
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive(&sm.empty_act[a]);
+      mbar_arrive(&sm.out_full[group][buf]);
+    }
+    if (epilogue) {
+      if (!warp_wait(&sm.out_full[group][buf], use & 1, p.wait_ns)) {
+        if (lane == 0) set_abort(sm);
+        break;
+      }
+      gated_rmsnorm_store<true>(o_buf, z, w, p.eps, lane, p.out + (bos * HV + head) * kDim);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.out_empty[group][buf]);
+    ++runs;
+  }
+}
+
+// Norm warp: for each of the CTA's items in order, wait until it lands, reduce its q and k norms and
+// arrive on the stage's `ready` barrier.  Measured on B200 (config 2, bf16 pool): done by the
+// producer after issuing the next item, every issue waited for the previous item's copies, so at
+// most two items were in flight (one item issued per 2.1 us against 1.8 us of work per item).
+__device__ void norm_loop(const DecodeArgs& p, Smem& sm, int lane) {
+  int k = 0;
+  for (int64_t item = blockIdx.x; item < p.total_items; item += gridDim.x, ++k) {
+    if (aborted(sm) || !publish_norms(p, sm, k, lane)) break;
+  }
+}
+
+// Block: two groups of 8 consumer warps, the producer warp and the norm warp; one CTA per SM.
+__global__ void __launch_bounds__(kThreads, 1) gdn_decode_b16_kernel(const DecodeArgs p) {
+  ldb::grid_dependency_wait();
+  ldb::allow_dependent_launch();
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    for (int s = 0; s < Smem::kStateStages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty_state[s], kGroupWarps);
+    }
+    for (int a = 0; a < Smem::kActStages; ++a) {
+      mbar_init(&sm.empty_act[a], kGroupWarps);
+      mbar_init(&sm.ready[a], 1);
+    }
+    for (int grp = 0; grp < kGroups; ++grp) {
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&sm.out_full[grp][b], kGroupWarps);
+        mbar_init(&sm.out_empty[grp][b], kGroupWarps);
+      }
+    }
+    sm.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  __syncthreads();
+  if (tid >= kGroups * kGroupThreads + 32) {
+    norm_loop(p, sm, tid & 31);
+  } else if (tid >= kGroups * kGroupThreads) {
+    produce(p, sm, tid & 31);
+  } else {
+    consume(p, sm, tid / kGroupThreads, tid % kGroupThreads);
+  }
+}
+
+}  // namespace b16
+
 }  // namespace stream
 
 bool aligned(const void* ptr, uintptr_t bytes) { return (reinterpret_cast<uintptr_t>(ptr) % bytes) == 0; }
@@ -1069,9 +1350,8 @@ int device_info(DeviceInfo& out) {
     err = cudaFuncSetAttribute(stream::gdn_decode_stream_kernel<4, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(sizeof(stream::Smem)));
     if (err == cudaSuccess) {
-      err = cudaFuncSetAttribute(stream::gdn_decode_stream_kernel<4, __nv_bfloat16>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(sizeof(stream::SmemT<__nv_bfloat16>)));
+      err = cudaFuncSetAttribute(stream::b16::gdn_decode_b16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(sizeof(stream::b16::Smem)));
     }
     if (err != cudaSuccess) return set_error(LD_ERR_CUDA, "shared-memory opt-in: %s", cudaGetErrorString(err));
     info.stream_ready = true;
@@ -1306,14 +1586,14 @@ extern "C" int ld_decode_bf16_state(const void* qkv, int64_t qkv_row_stride, con
   const bool bulk_ok = aligned(qkv, 16) && qkv_row_stride % 8 == 0 && aligned(gate, 16) &&
                        gate_row_stride % 8 == 0 && aligned(out, 8);
   const int forced = g_kernel_override.load(std::memory_order_relaxed);
-  const bool streaming = bulk_ok && (forced == LD_DECODE_KERNEL_STREAM ||
+  const bool streaming = bulk_ok && width == 1 && (forced == LD_DECODE_KERNEL_STREAM ||
                                      (forced != LD_DECODE_KERNEL_ROWREG && width == 1 &&
                                       args.total_items >= kStreamItemsPerSmBf16 * info.sms));
   cudaError_t err;
   if (streaming) {
     const dim3 grid(static_cast<unsigned int>(std::min<int64_t>(args.total_items, info.sms)));
-    err = ldb::launch(stream::gdn_decode_stream_kernel<4, __nv_bfloat16>, grid, dim3(Tile<4>::kThreads + 32),
-                      sizeof(stream::SmemT<__nv_bfloat16>), s, 1, args);
+    err = ldb::launch(stream::b16::gdn_decode_b16_kernel, grid, dim3(stream::b16::kThreads),
+                      sizeof(stream::b16::Smem), s, 1, args);
   } else {
     const bool vec_act = aligned(qkv, 8) && qkv_row_stride % 4 == 0 && aligned(gate, 8) &&
                          gate_row_stride % 4 == 0 && aligned(out, 8);

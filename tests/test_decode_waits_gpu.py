@@ -30,9 +30,10 @@ def streaming(device):
     capi.set_decode_wait_test(0, 0)
 
 
-@pytest.mark.parametrize("width", [1, 4])
-@pytest.mark.parametrize("state_dtype", ["fp32", "bf16"])
+@pytest.mark.parametrize("width, state_dtype", [(1, "fp32"), (4, "fp32"), (1, "bf16")])
 def test_waits_run_out_store_nothing_and_return(streaming, device, width, state_dtype):
+    """Both persistent kernels: the fp32 one (one-token and verify launches) and the bf16 pool's
+    one-token kernel (bf16 verify launches run the one-CTA-per-item kernel, which has no waits)."""
     case = workloads.make_decode_case(40, width, 1 + 40 * width + 5, device=device, seed=70 + width,
                                       accepted="uniform", state_scale=0.1)
     if state_dtype == "bf16":

@@ -150,7 +150,7 @@ int ld_copy_slots(float* pool, int64_t n_pool_slots, int64_t pool_slot_stride,
                   int64_t slot_elems, void* stream);
 
 /* Decode kernel variants (ld_decode_kernel_override). */
-#define LD_DECODE_KERNEL_AUTO 0        /* library default: STREAM for width-1 launches of >= 9 items per SM (>= 14 with a bf16 pool), else ROWREG */
+#define LD_DECODE_KERNEL_AUTO 0        /* library default: STREAM for width-1 launches of >= 9 items per SM (>= 7 with a bf16 pool), else ROWREG */
 #define LD_DECODE_KERNEL_ROWREG 1      /* one CTA per (request, head), state loaded into registers */
 #define LD_DECODE_KERNEL_STREAM 2      /* persistent kernel: TMA bulk loads into a 3-deep ring, 8 consumer warps */
 

@@ -22,7 +22,7 @@
 // 8 consumer warps run the recurrence on the register tile and store each step's state
 // straight from registers.  Up to three 64 KiB states per SM are in flight at all times, so
 // HBM never waits for a CTA's compute or store phase.  Every mbarrier wait is bounded
-// (LD_FAULT_WAIT_TIMEOUT).  No cluster and no multicast: each CTA reads only its own items
+// (LD_FAULT_WAIT_TIMEOUT).  No thread-block cluster: each CTA reads only its own items
 // from this GPU's memory.
 //
 // gdn_decode_rowreg_kernel: one CTA per item, loading the state straight into registers with
@@ -68,7 +68,7 @@ constexpr int kMaxTokens = LD_MAX_WIDTH;
 // One-token launches with at least this many (request, head) items per SM use the streaming
 // kernel (fp32 and bf16 pools); smaller ones and multi-token verify use one CTA per item.
 constexpr int kStreamItemsPerSm = 9;
-constexpr int kStreamItemsPerSmBf16 = 14;
+constexpr int kStreamItemsPerSmBf16 = 7;
 
 __device__ unsigned int g_decode_faults;
 
@@ -625,7 +625,7 @@ __device__ __noinline__ bool mbar_wait(unsigned long long* bar, uint32_t parity,
   return true;
 }
 
-// Non-multicast TMA bulk copy global -> this CTA's shared memory, completing on `bar`.
+// TMA bulk copy global -> this CTA's own shared memory (one destination), completing on `bar`.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, unsigned long long* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                    smem_u32(dst)),
@@ -1580,9 +1580,11 @@ extern "C" int ld_decode_bf16_state(const void* qkv, int64_t qkv_row_stride, con
   rc = device_info(info);
   if (rc != LD_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // The streaming and one-CTA-per-item kernels have bf16-state forms.  With half the state bytes
-  // the one-CTA-per-item kernel stays ahead to larger one-token launches (measured on B200,
-  // HV=32: 2,048 items 35.4 vs 35.8 us, 3,072 items 60.3 vs 52.5 us, config 2 164 vs 131 us).
+  // One-token launches of at least 7 items per SM run the two-group streaming kernel, smaller ones
+  // and multi-token launches the one-CTA-per-item kernel.  Measured on B200 (HV=32, CUDA-graph
+  // replay, T=1): 1,024 items 17.2 (one CTA per item) vs 17.0 us, 2,048 items 32.4 vs 28.7 us,
+  // 4,096 items 72.6 vs 54.3 us; at T=4 (config 3) 71.2 us against 75.2 us for a multi-token form
+  // of the streaming kernel, which was not kept.
   const bool bulk_ok = aligned(qkv, 16) && qkv_row_stride % 8 == 0 && aligned(gate, 16) &&
                        gate_row_stride % 8 == 0 && aligned(out, 8);
   const int forced = g_kernel_override.load(std::memory_order_relaxed);

@@ -70,6 +70,8 @@ def parse_args(argv=None):
                    help="decode kernel variant (all compute the same results)")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline budget (rank 0, N=1)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-compare", action="store_true",
+                   help="conv workload: skip the vLLM conv + decode comparison pipeline")
     p.add_argument("--no-extras", action="store_true",
                    help="skip the secondary configs (3, 4, bf16 pool) that the default decode line also reports")
     args = p.parse_args(argv)
@@ -320,7 +322,7 @@ def build_workload(name: str, args, dist: Dist, device, stream) -> Workload:
         config = {"workload": "config2_conv_decode", "sequences_per_gpu": requests, "tokens_per_sequence": width,
                   "num_k_heads": h, "num_v_heads": hv, "conv_width": conv_width, "conv_state_dtype": "bf16",
                   "conv_layout": "[slots, dim, L]", "launches_per_step": "conv update + decode",
-                  "vllm_pipeline": unfused_conv_decode_us(case, conv, stream)}
+                  "vllm_pipeline": None if args.no_compare else unfused_conv_decode_us(case, conv, stream)}
         # The two kernels (conv update, decode) are accounted together as one step.
         return Workload(fn, workloads.decode_algorithmic_bytes(requests, width, case.tokens, h, hv) + conv_bytes,
                         requests * 2 * hv * workloads.SLOT_HEAD_BYTES, case.tokens, "tokens/s", config,
@@ -400,9 +402,10 @@ EXTRA_WORKLOADS = ("verify", "copy", "decode_bf16", "verify_bf16")
 def measure(w: Workload, steps: int, warmup: int, dist: Dist, stream, peaks: dict) -> dict:
     total_ms, launch_ms, window = timed_launches(w.fn, steps, warmup, dist, stream)
     max_ms = dist.max(total_ms)
+    min_ms = -dist.max(-total_ms)
     kernel_ms = launch_ms / w.launches_per_step
     achieved = w.bytes_per_launch / (kernel_ms * 1e-3) / 1e9
-    return {"total_ms": total_ms, "max_ms": max_ms, "kernel_ms": kernel_ms, "achieved_gbs": achieved,
+    return {"total_ms": total_ms, "max_ms": max_ms, "min_ms": min_ms, "kernel_ms": kernel_ms, "achieved_gbs": achieved,
             "frac": achieved / peaks["hbm_gbs"], "window": window,
             "value": dist.sum(w.units_per_step) * steps / (max_ms * 1e-3),
             "state_gbs": dist.sum(w.bytes_per_launch * w.launches_per_step * steps / (total_ms * 1e-3) / 1e9)}
@@ -468,6 +471,7 @@ def run_ours(args, dist: Dist) -> dict | None:
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": m["max_ms"] / args.steps,
+        "rank_ms_per_step": {"min": m["min_ms"] / args.steps, "max": m["max_ms"] / args.steps},
         "higher_is_better": True,
         "scaling": "strong" if args.workload == "stacked" else "weak",
         "vs_baseline": None,

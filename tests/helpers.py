@@ -14,12 +14,23 @@ from golden import cases
 # States must meet the tighter reference pool tolerance (which implies the north-star one).
 # bf16 outputs must meet the reference test tolerance everywhere and the north-star tolerance
 # everywhere except at rounding-boundary flips: elements that differ by exactly one bf16 ulp
-# (the fp32 recurrence output landing on the other side of a bf16 rounding boundary) and make
-# up at most 0.1% of the elements.
+# (the fp32 recurrence output landing on the other side of a bf16 rounding boundary).
+# Outlier bounds are about 2-3x the largest rate measured on B200 over the whole GPU suite (the
+# run's terminal summary prints them), with a floor of one element (two for the looser forms) so
+# that a case with a few thousand outputs can hold the single flip its larger siblings show:
+#   outputs outside 2e-3                          measured 7.6e-6   bound 2e-5
+#   outputs outside 2e-3 downstream of the conv   measured 2.0e-5   bound 5e-5
+#   bf16-pool states one ulp apart                measured 5.5e-5   bound 1.2e-4
 STATE_ATOL, STATE_RTOL = 3e-6, 3e-4
 NORTH_ATOL, NORTH_RTOL = 2e-3, 2e-3
 OUT_REF_ATOL, OUT_REF_RTOL = 0.008, 0.02
-MAX_FLIP_FRACTION = 1e-3
+MAX_FLIP_FRACTION = 2e-5
+MAX_TAIL_FRACTION = 5e-5
+
+
+def allowed(size: int, fraction: float, floor: int = 1) -> float:
+    """Outliers a check of `size` elements may hold at `fraction`."""
+    return max(floor, fraction * size)
 
 # Measured outlier rates of every tolerance check in this session (printed at the end of the run
 # by tests/conftest.py), so the bounds above can be kept close to what the kernels achieve.
@@ -60,7 +71,8 @@ def assert_out_close(actual_bits: np.ndarray, expected_bits: np.ndarray, what: s
                                        f"({int(outliers.sum())} outside 2e-3)")
     fraction = outliers.mean() if outliers.size else 0.0
     MEASURED.append(("out", what, int(outliers.sum()), int(outliers.size), worst))
-    assert fraction <= max_fraction, f"{what}: {outliers.sum()} rounding flips ({fraction:.2e} of elements)"
+    assert outliers.sum() <= allowed(outliers.size, max_fraction), \
+        f"{what}: {outliers.sum()} rounding flips ({fraction:.2e} of elements)"
     return dict(elements=int(actual.size), exact=int((ulps == 0).sum()), one_ulp=int((ulps == 1).sum()),
                 outside_2e3=int(outliers.sum()), outlier_ulps=worst, max_diff=float(diff.max()) if diff.size else 0.0)
 
@@ -69,7 +81,7 @@ def assert_out_close(actual_bits: np.ndarray, expected_bits: np.ndarray, what: s
 # stored step to bf16, so their fp32 values (within 3e-6 / 3e-4 of each other) round to the same
 # bf16 value except where they straddle a rounding boundary (one ulp apart) or where a value
 # near zero has bf16 ulps finer than the fp32 tolerance (then the fp32 tolerance applies).
-BF16_STATE_MAX_FLIP_FRACTION = 1e-2
+BF16_STATE_MAX_FLIP_FRACTION = 1.2e-4
 
 
 def assert_bf16_state_close(actual_bits: np.ndarray, expected_bits: np.ndarray, what: str = "bf16 state",
@@ -91,7 +103,8 @@ def assert_bf16_state_close(actual_bits: np.ndarray, expected_bits: np.ndarray, 
                              f"3e-6 / 3e-4 apart (actual, expected): {worst}")
     fraction = float((ulps >= 1).mean()) if ulps.size else 0.0
     MEASURED.append(("bf16 state", what, int((ulps >= 1).sum()), int(ulps.size), int(ulps.max()) if ulps.size else 0))
-    assert fraction <= BF16_STATE_MAX_FLIP_FRACTION, f"{what}: {int((ulps >= 1).sum())} differ ({fraction:.2e})"
+    assert (ulps >= 1).sum() <= allowed(ulps.size, BF16_STATE_MAX_FLIP_FRACTION, 2), \
+        f"{what}: {int((ulps >= 1).sum())} differ ({fraction:.2e})"
     return dict(elements=int(ulps.size), one_ulp=int((ulps == 1).sum()), more=int((ulps > 1).sum()),
                 max_diff=float(diff.max()) if diff.size else 0.0)
 
@@ -116,13 +129,13 @@ CONV_STATE_OUTLIER_ATOL = 1e-2
 
 def assert_out_close_after_conv(actual_bits: np.ndarray, expected_bits: np.ndarray, what: str = "out") -> dict:
     """Outputs computed from post-conv q, k, v: every element within the reference test's
-    0.008 / 0.02, and at most 1e-3 of them outside 2e-3.  A post-conv q or k value that rounds
+    0.008 / 0.02, and at most MAX_TAIL_FRACTION of them outside 2e-3.  A post-conv q or k value that rounds
     one ulp apart shifts its whole normalised row, so near-zero outputs can move by a few ulps."""
     return assert_out_close_tail(actual_bits, expected_bits, what)
 
 
 def assert_out_close_tail(actual_bits: np.ndarray, expected_bits: np.ndarray, what: str = "out") -> dict:
-    """Every element within the reference test's 0.008 / 0.02 and at most 1e-3 of them outside
+    """Every element within the reference test's 0.008 / 0.02 and at most MAX_TAIL_FRACTION of them outside
     2e-3, without the one-ulp bound on those few: for inputs whose recurrence outputs sit near a
     bf16 rounding boundary (the output is rounded to bf16 before the gated RMSNorm), a one-ulp
     flip there is scaled by the norm and can land two ulps apart after the final rounding."""
@@ -137,7 +150,8 @@ def assert_out_close_tail(actual_bits: np.ndarray, expected_bits: np.ndarray, wh
     ulps = bf16_ulp_distance(actual_bits, expected_bits)
     MEASURED.append(("out tail", what, int(outliers.sum()), int(outliers.size),
                      int(ulps[outliers].max()) if outliers.any() else 0))
-    assert fraction <= MAX_FLIP_FRACTION, f"{what}: {outliers.sum()} elements outside 2e-3 ({fraction:.2e})"
+    assert outliers.sum() <= allowed(outliers.size, MAX_TAIL_FRACTION, 2), \
+        f"{what}: {outliers.sum()} elements outside 2e-3 ({fraction:.2e})"
     return dict(outside_2e3=int(outliers.sum()), max_diff=float(diff.max()) if diff.size else 0.0)
 
 
@@ -147,6 +161,7 @@ def assert_state_close_after_conv(actual: np.ndarray, expected: np.ndarray, what
     diff = np.abs(actual - expected)
     ok = diff <= STATE_ATOL + STATE_RTOL * np.abs(expected)
     fraction = float((~ok).mean()) if ok.size else 0.0
+    MEASURED.append(("state after conv", what, int((~ok).sum()), int(ok.size), 0))
     assert fraction <= CONV_STATE_OUTLIER_FRACTION, f"{what}: {int((~ok).sum())} of {ok.size} outside 3e-6 / 3e-4"
     assert (diff <= CONV_STATE_OUTLIER_ATOL).all(), f"{what}: max diff {diff.max()} above {CONV_STATE_OUTLIER_ATOL}"
     return dict(outside=int((~ok).sum()), max_diff=float(diff.max()) if diff.size else 0.0)

@@ -27,8 +27,8 @@ PHYSICAL_POOLS = 5
 LAYERS_PER_POOL = -(-LAYERS // PHYSICAL_POOLS)
 SLOTS_PER_LAYER = SEQUENCES * WIDTH
 POOL_SLOTS = 1 + LAYERS_PER_POOL * SLOTS_PER_LAYER
-# Outputs outside 2e-3 of the oracle over 48 layers: a first run measured 4 of 12.6 M (3.2e-7); the
-# bound is about three times that rate and far below the single-config bound (1e-3).
+# Outputs outside 2e-3 of the oracle over 48 layers: runs measured 4 of 12.6 M (3.2e-7) and 2 of
+# 6.3 M; the bound is about three times that rate.
 OUTLIER_FRACTION = 1e-6
 
 
@@ -96,7 +96,7 @@ def test_stacked_graph_replays_match_the_oracle(device):
             # output that lands on a bf16 rounding boundary before the gated RMSNorm (which scales
             # the flip) can end two ulps from the oracle.
             stats = assert_out_close(bits(c.out), expected[index], f"replay {replay} layer {index} out",
-                                     max_outlier_ulps=2, max_fraction=1e-4)
+                                     max_outlier_ulps=2, max_fraction=2e-5)
             flips += stats["outside_2e3"]
             worst = max(worst, stats["outlier_ulps"])
         total = LAYERS * SEQUENCES * WIDTH * 32 * 128

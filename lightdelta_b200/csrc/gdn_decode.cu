@@ -53,7 +53,6 @@ namespace {
 
 constexpr int kDim = LD_HEAD_DIM;                      // K = V = 128
 constexpr int kHeadElems = kDim * kDim;                // floats per (slot, value head)
-constexpr int kHeadBytes = kHeadElems * 4;             // 65,536
 constexpr int kRowBytes = kDim * 2;                    // one bf16 head row: 256 B
 constexpr int kLanesPerRow = 8;                        // lanes sharing one state row
 constexpr int kVecPerRow = kDim / (4 * kLanesPerRow);  // float4 per lane per row: 4
@@ -551,34 +550,24 @@ struct ActStage {
   ItemInfo info;
 };
 
-// State ring of the streaming kernel: three 64 KiB fp32 stages, or six 32 KiB bf16 ones (the same
-// bytes in flight), each with an activation stage behind it.
-template <typename StateT>
-struct SmemT {
-  using State = StateT;
-  static constexpr int kStateStages = sizeof(StateT) == 4 ? kStates : 2 * kStates;
+// State ring of the fp32 streaming kernel: three 64 KiB stages, each with an activation stage
+// behind it.  The consumer warps reduce the q / k norms themselves: done by the producer, its waits
+// for each item's data cost 175.2 -> 192.1 us on config 2 (B200).
+struct Smem {
+  using State = float;
+  static constexpr int kStateStages = kStates;
   static constexpr int kActStages = kStateStages + 1;
-  // bf16 pools: the producer reduces each token's q / k norms once and publishes them (`ready`)
-  // instead of every consumer warp reducing them.  Measured on B200, config 2: bf16 pool 129.3 ->
-  // 122.7 us; with the fp32 pool the producer's extra waits cost 175.2 -> 192.1 us, so there the
-  // consumers keep the reduction.  The producer publishes item k's norms after issuing item
-  // k + kNormLag (lag 1: 122.7 us, lag 3: 124.7 us).
-  static constexpr bool kProducerNorms = sizeof(StateT) == 2;
-  static constexpr int kNormLag = 1;
-  StateT state[kStateStages][kHeadElems];
+  float state[kStateStages][kHeadElems];
   ActStage act[kActStages];
   float out[2][kMaxTokens][kDim];
   unsigned long long full[kStateStages];
   unsigned long long empty_state[kStateStages];
   unsigned long long empty_act[kActStages];
-  unsigned long long ready[kActStages];  // the producer wrote the stage's q / k norms
   unsigned long long out_full[2];   // all consumer warps wrote their rows of out[b]
   unsigned long long out_empty[2];  // all consumer warps are past the epilogue that read out[b]
   int abort;
 };
-using Smem = SmemT<float>;
-static_assert(sizeof(SmemT<float>) <= 227 * 1024 && sizeof(SmemT<__nv_bfloat16>) <= 227 * 1024,
-              "the streaming kernel's ring must fit one CTA's shared memory");
+static_assert(sizeof(Smem) <= 227 * 1024, "the streaming kernel's ring must fit one CTA's shared memory");
 
 __device__ __forceinline__ uint32_t smem_u32(const void* ptr) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
@@ -820,17 +809,8 @@ __device__ void produce(const DecodeArgs& p, S& sm, int lane) {
       }
     }
     __syncwarp();
-    if constexpr (S::kProducerNorms) {
-      if (k >= S::kNormLag && !publish_norms(p, sm, k - S::kNormLag, lane)) break;
-    }
   }
-  // Norms of the last items, then drain: every bulk copy this warp issued has landed before the
-  // CTA may exit.
-  if constexpr (S::kProducerNorms) {
-    for (int kk = k > S::kNormLag ? k - S::kNormLag : 0; kk < k; ++kk) {
-      if (!publish_norms(p, sm, kk, lane)) break;
-    }
-  }
+  // Drain: every bulk copy this warp issued has landed before the CTA may exit.
   if (lane == 0) {
     for (int kk = k > kStates ? k - kStates : 0; kk < k; ++kk) {
       if (!mbar_wait(&sm.full[kk % kStates], (kk / kStates) & 1, p.wait_ns)) {
@@ -869,7 +849,6 @@ __device__ void consume(const DecodeArgs& p, S& sm, int tid) {
   constexpr int kActs = S::kActStages;
   using State = typename S::State;
   constexpr int kConsumers = Tile<kRows>::kThreads;
-  constexpr int kConsumerWarps = kConsumers / 32;
   constexpr int kRowGroups = Tile<kRows>::kRowGroups;
   const int HV = p.num_v_heads;
   const int lane = tid & 31;
@@ -885,10 +864,6 @@ __device__ void consume(const DecodeArgs& p, S& sm, int tid) {
     const int s = k % kStates;
     const int a = k % kActs;
     if (!warp_wait(&sm.full[s], (k / kStates) & 1, p.wait_ns)) {
-      if (lane == 0) set_abort(sm);
-      break;
-    }
-    if (S::kProducerNorms && !warp_wait(&sm.ready[a], (k / kActs) & 1, p.wait_ns)) {
       if (lane == 0) set_abort(sm);
       break;
     }
@@ -931,29 +906,18 @@ __device__ void consume(const DecodeArgs& p, S& sm, int tid) {
     for (int t = 0; t < n; ++t) {
       float4 kv[kVecPerRow], qv[kVecPerRow];
       float k_sq, q_sq;
-      load_row_cols<sizeof(State) == 2>(act.k[t], j, kv, k_sq);
-      load_row_cols<sizeof(State) == 2>(act.q[t], j, qv, q_sq);
-      // L2 norms in fp32 as gdn.py:98-99; q then scaled by K^-1/2 as gdn.py:101.  With a bf16
-      // pool the producer has reduced them already.
-      if constexpr (S::kProducerNorms) {
-        const float k_inv = info.k_inv[t];
-        const float q_inv = info.q_inv[t];
+      load_row_cols<false>(act.k[t], j, kv, k_sq);
+      load_row_cols<false>(act.q[t], j, qv, q_sq);
+      // L2 norms in fp32 as gdn.py:98-99; q then scaled by K^-1/2 as gdn.py:101.
+      k_sq = row_sum(k_sq);
+      q_sq = row_sum(q_sq);
+      const float k_inv = 1.0f / sqrtf(k_sq + 1e-6f);
+      const float q_inv = 1.0f / sqrtf(q_sq + 1e-6f);
 #pragma unroll
-        for (int c = 0; c < kVecPerRow; ++c) {
-          kv[c] = make_float4(kv[c].x * k_inv, kv[c].y * k_inv, kv[c].z * k_inv, kv[c].w * k_inv);
-          qv[c] = make_float4(qv[c].x * q_inv, qv[c].y * q_inv, qv[c].z * q_inv, qv[c].w * q_inv);
-        }
-      } else {
-        k_sq = row_sum(k_sq);
-        q_sq = row_sum(q_sq);
-        const float k_inv = 1.0f / sqrtf(k_sq + 1e-6f);
-        const float q_inv = 1.0f / sqrtf(q_sq + 1e-6f);
-#pragma unroll
-        for (int c = 0; c < kVecPerRow; ++c) {
-          kv[c] = make_float4(kv[c].x * k_inv, kv[c].y * k_inv, kv[c].z * k_inv, kv[c].w * k_inv);
-          qv[c] = make_float4(qv[c].x * q_inv * p.q_scale, qv[c].y * q_inv * p.q_scale,
-                              qv[c].z * q_inv * p.q_scale, qv[c].w * q_inv * p.q_scale);
-        }
+      for (int c = 0; c < kVecPerRow; ++c) {
+        kv[c] = make_float4(kv[c].x * k_inv, kv[c].y * k_inv, kv[c].z * k_inv, kv[c].w * k_inv);
+        qv[c] = make_float4(qv[c].x * q_inv * p.q_scale, qv[c].y * q_inv * p.q_scale,
+                            qv[c].z * q_inv * p.q_scale, qv[c].w * q_inv * p.q_scale);
       }
       float vrow[kRows], o[kRows];
 #pragma unroll
@@ -970,13 +934,9 @@ __device__ void consume(const DecodeArgs& p, S& sm, int tid) {
         store_tile<kRows>(state_base<State>(p) + static_cast<int64_t>(dst) * p.slot_stride + head_offset, g, j, tile);
       }
     }
-    // Token et's gated RMSNorm runs on warp et, or with a bf16 pool on warp (runs + et) mod
-    // kConsumerWarps, moving round the warps from item to item.  Measured on B200 (config 2,
-    // 256 x T=1, HV=32): rotating takes the bf16 pool from 141.9 to 132.1 us, where the compute
-    // per item is the bound and warp 0 was the slowest; with the HBM-bound fp32 pool it costs
-    // 175 -> 192 us, so the fp32 pool keeps the fixed assignment.
-    constexpr bool kRotateEpilogue = sizeof(State) == 2;
-    const int et = kRotateEpilogue ? (warp + kConsumerWarps - runs % kConsumerWarps) % kConsumerWarps : warp;
+    // Token et's gated RMSNorm runs on warp et (rotating it over the warps from item to item cost
+    // 175 -> 192 us on config 2: with the HBM-bound fp32 pool the first warps have slack).
+    const int et = warp;
     float z[4] = {0.f, 0.f, 0.f, 0.f};
     if (et < n) {
       const uint2 raw = *reinterpret_cast<const uint2*>(&act.z[et][4 * lane]);
@@ -1006,13 +966,13 @@ __device__ void consume(const DecodeArgs& p, S& sm, int tid) {
 // Block: Tile<kRows>::kThreads consumer threads followed by one producer warp, one CTA per SM.
 // The register cap keeps the block launchable: its 9 warps are spread over the SM's four 16 K-register
 // sub-partitions (at most 3 warps each), which allows 168 registers per thread.
-template <int kRows, typename StateT>
+template <int kRows>
 __global__ void __maxnreg__(168) gdn_decode_stream_kernel(const DecodeArgs p) {
   ldb::grid_dependency_wait();
   ldb::allow_dependent_launch();
   constexpr int kConsumers = Tile<kRows>::kThreads;
   constexpr int kConsumerWarps = kConsumers / 32;
-  using S = SmemT<StateT>;
+  using S = Smem;
   constexpr int kStates = S::kStateStages;
   constexpr int kActs = S::kActStages;
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -1023,10 +983,7 @@ __global__ void __maxnreg__(168) gdn_decode_stream_kernel(const DecodeArgs p) {
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty_state[s], kConsumerWarps);
     }
-    for (int a = 0; a < kActs; ++a) {
-      mbar_init(&sm.empty_act[a], kConsumerWarps);
-      mbar_init(&sm.ready[a], 1);
-    }
+    for (int a = 0; a < kActs; ++a) mbar_init(&sm.empty_act[a], kConsumerWarps);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sm.out_full[b], kConsumerWarps);
       mbar_init(&sm.out_empty[b], kConsumerWarps);
@@ -1075,14 +1032,12 @@ struct ActStage1 {
 };
 
 // The producer's view (produce() / publish_norms()) plus per-group output buffers.  The producer
-// only issues copies (kProducerNorms is false: it never waits for data); a norm warp of its own
-// publishes each item's q / k norms as soon as the item lands (norm_loop).
+// only issues copies (it never waits for data); a norm warp of its own publishes each item's q / k
+// norms on `ready` as soon as the item lands (norm_loop).
 struct Smem {
   using State = __nv_bfloat16;
   static constexpr int kStateStages = 6;
   static constexpr int kActStages = 8;
-  static constexpr bool kProducerNorms = false;
-  static constexpr int kNormLag = 1;
   __nv_bfloat16 state[kStateStages][kHeadElems];
   ActStage1 act[kActStages];
   float out[kGroups][2][kDim];
@@ -1347,7 +1302,7 @@ int device_info(DeviceInfo& out) {
   if (!info.stream_ready) {
     err = cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, device);
     if (err != cudaSuccess) return set_error(LD_ERR_CUDA, "SM count: %s", cudaGetErrorString(err));
-    err = cudaFuncSetAttribute(stream::gdn_decode_stream_kernel<4, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    err = cudaFuncSetAttribute(stream::gdn_decode_stream_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(sizeof(stream::Smem)));
     if (err == cudaSuccess) {
       err = cudaFuncSetAttribute(stream::b16::gdn_decode_b16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1513,7 +1468,7 @@ extern "C" int ld_decode(const void* qkv, int64_t qkv_row_stride, const void* a,
   cudaError_t err;
   if (variant == LD_DECODE_KERNEL_STREAM) {
     const dim3 grid(static_cast<unsigned int>(std::min<int64_t>(args.total_items, info.sms)));
-    err = ldb::launch(stream::gdn_decode_stream_kernel<4, float>, grid, dim3(Tile<4>::kThreads + 32),
+    err = ldb::launch(stream::gdn_decode_stream_kernel<4>, grid, dim3(Tile<4>::kThreads + 32),
                       sizeof(stream::Smem), s, 1, args);
   } else {
     const bool vec_act = aligned(qkv, 8) && qkv_row_stride % 4 == 0 && aligned(gate, 8) &&

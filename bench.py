@@ -432,9 +432,10 @@ def run_ours(args, dist: Dist) -> dict | None:
     e2e = None
     if args.workload in ("decode", "verify"):
         e2e = run_e2e(case, args, dist, stream)
-    cpu = None
+    cpu = cpu_torch = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline and args.workload in ("decode", "verify"):
         cpu = cpu_baseline(case, args.cpu_seconds)
+        cpu_torch = torch_reference_baseline(case, args.cpu_seconds)
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline and args.workload == "sample":
         cpu = sampling_cpu_baseline(w.sampling, args.cpu_seconds)
     if w.cleanup is not None:
@@ -495,6 +496,7 @@ def run_ours(args, dist: Dist) -> dict | None:
         },
         "e2e": e2e,
         "cpu_baseline": cpu,
+        "cpu_baseline_reference_torch": cpu_torch,
         "gpu_launches": main["kernels_per_step"] * args.steps,
         "clocks": clocks,
     }
@@ -678,6 +680,46 @@ def cpu_baseline(case, seconds: float) -> dict:
                       f"{elapsed:.1f} s, C oracle with OpenMP"}
 
 
+def torch_reference_baseline(case, seconds: float, requests: int | None = None) -> dict:
+    """The reference's own CPU implementation (oracle/ref_torch.py: its post_conv_gdn, compiled
+    unmodified, with GDNBackend's packed gather and commit) on the same host workload as the C port,
+    repeated for ~`seconds` with torch's default CPU threads."""
+    import numpy as np
+    import torch
+
+    from oracle import ref_torch
+
+    if not ref_torch.available():
+        return {"unavailable": "oracle/_ref/py not built (python oracle/build_ref.py, where the reference exists)"}
+    w = host_workload(case, requests)
+
+    def bf16(x):
+        return torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).view(torch.bfloat16)
+
+    args = dict(qkv=bf16(w["qkv"]), a=bf16(w["a"]), b=bf16(w["b"]), a_log=torch.from_numpy(w["a_log"]),
+                dt_bias=torch.from_numpy(w["dt_bias"]), slots=torch.from_numpy(w["slots"]),
+                cu=torch.from_numpy(w["cu"]), accepted=torch.from_numpy(w["accepted"]),
+                pool=torch.from_numpy(w["pool"]), gate=bf16(w["gate"]), weight=bf16(w["weight"]),
+                out=torch.zeros(w["out"].shape, dtype=torch.bfloat16))
+
+    def step():
+        ref_torch.packed_decode(**args, num_k_heads=w["num_k_heads"])
+
+    step()  # warm-up
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        step()
+        reps += 1
+        elapsed = time.perf_counter() - t0
+        if elapsed >= seconds:
+            break
+    return {"value": w["tokens"] * reps / elapsed, "unit": "tokens/s", "cores": torch.get_num_threads(),
+            "kind": "reference",
+            "sample": f"{w['requests']} sequences ({w['tokens']} tokens) per step x {reps} steps, {elapsed:.1f} s, "
+                      f"the reference's post_conv_gdn (python/lightdelta/reference/gdn.py:70-128) with "
+                      f"GDNBackend's packed gather and commit (backend.py:30-91), torch {torch.__version__} CPU"}
+
+
 def unfused_conv_decode_us(case, conv, stream) -> dict | None:
     """Device time per step of the pipeline conv_decode replaces: vLLM's causal_conv1d_update
     (Triton) then lightdelta::decode, as vllm_layer.py:199-220 runs them; None without vLLM."""
@@ -857,6 +899,7 @@ def run_reference(args, dist: Dist) -> dict | None:
                    "parallelism": "rank 0 host CPU only"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "reference_torch": torch_reference_baseline(case, args.cpu_seconds),
         "reference_gpu_kernel": reference_gpu_kernel(args.steps, args.warmup),
     }
 

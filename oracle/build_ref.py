@@ -13,6 +13,11 @@ the reference's csrc/gdn_decode.cu unmodified and launches its kernel template a
 kernel can run at the BASELINE geometry (H=16, HV=32).  It registers no torch operators, so it
 can share a process with lightdelta_b200.
 
+And it byte-compiles the reference's torch decode path -- python/lightdelta/__init__.py and
+python/lightdelta/reference/{__init__,gdn}.py, unmodified -- into sourceless .pyc files under
+oracle/_ref/py/lightdelta/ (an importable package for this interpreter), so that the reference's own
+CPU implementation can be timed on a host where the reference tree is absent (oracle/ref_torch.py).
+
 Run here (where the reference sources exist):  python oracle/build_ref.py [--reference DIR]
 """
 
@@ -100,12 +105,36 @@ def build_harness(reference: Path = DEFAULT_REFERENCE, force: bool = False) -> P
     return HARNESS
 
 
+TORCH_PATH_DIR = OUT_DIR / "py"
+TORCH_PATH_MODULES = ("lightdelta/__init__.py", "lightdelta/reference/__init__.py", "lightdelta/reference/gdn.py")
+
+
+def build_torch_path(reference: Path = DEFAULT_REFERENCE, force: bool = False) -> Path:
+    """Compiles the reference's torch path to bytecode, one .pyc beside where each source would be
+    (the layout Python imports without sources).  Only these three modules: the package marker and
+    post_conv_gdn, which import nothing of the reference beyond each other."""
+    import py_compile
+
+    for module in TORCH_PATH_MODULES:
+        src = reference / "python" / module
+        if not src.exists():
+            raise FileNotFoundError(f"reference module not found: {src}")
+        dst = TORCH_PATH_DIR / (module[: -len(".py")] + ".pyc")
+        if dst.exists() and not force and src.stat().st_mtime <= dst.stat().st_mtime:
+            continue
+        dst.parent.mkdir(parents=True, exist_ok=True)
+        py_compile.compile(str(src), cfile=str(dst), doraise=True,
+                           invalidation_mode=py_compile.PycInvalidationMode.UNCHECKED_HASH)
+    return TORCH_PATH_DIR
+
+
 def build_if_available() -> Path | None:
-    """Builds oracle/_ref/_C.so when the reference sources are present (this container); on the
-    GPU box the prebuilt library is used as shipped."""
+    """Builds oracle/_ref/_C.so (and the harness and the torch path's bytecode) when the reference
+    sources are present (this container); on the GPU box the prebuilt files are used as shipped."""
     if not DEFAULT_REFERENCE.exists():
         return OUT if OUT.exists() else None
     build_harness(DEFAULT_REFERENCE)
+    build_torch_path(DEFAULT_REFERENCE)
     return build(DEFAULT_REFERENCE)
 
 
@@ -116,6 +145,7 @@ def main() -> int:
     args = parser.parse_args()
     print(build(args.reference, args.force))
     print(build_harness(args.reference, args.force))
+    print(build_torch_path(args.reference, args.force))
     return 0
 
 

@@ -29,6 +29,7 @@ def test_defaults_are_the_headline_workload():
 def test_reference_arm_prints_one_contract_line():
     env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
     result = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "3",
+                             "--cpu-seconds", "2",
                              "--warmup", "3"], capture_output=True, text=True, timeout=600, env=env, check=True)
     lines = [line for line in result.stdout.splitlines() if line.strip()]
     assert len(lines) == 1
@@ -39,6 +40,9 @@ def test_reference_arm_prints_one_contract_line():
     assert line["impl"] == "reference" and line["unit"] == "tokens/s" and line["value"] > 0
     assert line["metric"] == bench.METRIC
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+    torch_path = line["reference_torch"]
+    if "unavailable" not in torch_path:
+        assert torch_path["kind"] == "reference" and torch_path["value"] > 0 and torch_path["cores"] >= 1
     assert line["e2e"] == {"value": line["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
     assert line["config"]["workload"] == "config2_decode"

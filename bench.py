@@ -683,15 +683,18 @@ def cpu_baseline(case, seconds: float) -> dict:
 def torch_reference_baseline(case, seconds: float, requests: int | None = None) -> dict:
     """The reference's own CPU implementation (oracle/ref_torch.py: its post_conv_gdn, compiled
     unmodified, with GDNBackend's packed gather and commit) on the same host workload as the C port,
-    repeated for ~`seconds` with torch's default CPU threads."""
+    repeated for ~`seconds` on every host thread this process may use."""
     import numpy as np
     import torch
 
+    import oracle
     from oracle import ref_torch
 
     if not ref_torch.available():
         return {"unavailable": "oracle/_ref/py not built (python oracle/build_ref.py, where the reference exists)"}
     w = host_workload(case, requests)
+    saved_threads = torch.get_num_threads()
+    torch.set_num_threads(oracle.default_threads())
 
     def bf16(x):
         return torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).view(torch.bfloat16)
@@ -705,16 +708,19 @@ def torch_reference_baseline(case, seconds: float, requests: int | None = None) 
     def step():
         ref_torch.packed_decode(**args, num_k_heads=w["num_k_heads"])
 
-    step()  # warm-up
-    reps, t0 = 0, time.perf_counter()
-    while True:
-        step()
-        reps += 1
-        elapsed = time.perf_counter() - t0
-        if elapsed >= seconds:
-            break
-    return {"value": w["tokens"] * reps / elapsed, "unit": "tokens/s", "cores": torch.get_num_threads(),
-            "kind": "reference",
+    try:
+        step()  # warm-up
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            step()
+            reps += 1
+            elapsed = time.perf_counter() - t0
+            if elapsed >= seconds:
+                break
+        threads = torch.get_num_threads()
+    finally:
+        torch.set_num_threads(saved_threads)
+    return {"value": w["tokens"] * reps / elapsed, "unit": "tokens/s", "cores": threads, "kind": "reference",
             "sample": f"{w['requests']} sequences ({w['tokens']} tokens) per step x {reps} steps, {elapsed:.1f} s, "
                       f"the reference's post_conv_gdn (python/lightdelta/reference/gdn.py:70-128) with "
                       f"GDNBackend's packed gather and commit (backend.py:30-91), torch {torch.__version__} CPU"}
@@ -844,6 +850,56 @@ def reference_gpu_kernel(steps: int, warmup: int) -> dict:
     return result
 
 
+def reference_copy(args, dist: Dist) -> dict:
+    """Config 4 on the host: the reference's CPU state I/O is torch indexing -- GDNBackend's packed
+    gather is index_select into the packed buffer and its commit index_copy_ into the pool
+    (python/lightdelta/backend.py:40-44, :87-91; its gather_state / scatter_state ops are CUDA-only).
+    One step gathers 128 distinct slots of a 257-slot pool and scatters them to 128 others (2 MiB
+    slots, 0.5 GiB moved per op), on every host thread this process may use."""
+    import torch
+
+    import oracle
+
+    slots = 128
+    threads = oracle.default_threads()
+    saved_threads = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    try:
+        gen = torch.Generator().manual_seed(4)
+        pool = torch.empty(2 * slots + 1, 32, 128, 128)
+        pool.normal_(0.0, 0.02, generator=gen)
+        perm = torch.randperm(2 * slots, generator=gen) + 1
+        gather_idx, scatter_idx = perm[:slots], perm[slots:]
+        packed = torch.empty(slots, 32, 128, 128)
+
+        def step():
+            torch.index_select(pool, 0, gather_idx, out=packed)
+            pool.index_copy_(0, scatter_idx, packed)
+
+        for _ in range(args.warmup):
+            step()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            step()
+        elapsed = time.perf_counter() - t0
+    finally:
+        torch.set_num_threads(saved_threads)
+    value = slots * args.steps / elapsed
+    sample = (f"{slots} of config 4's 512 slots per step from a {2 * slots + 1}-slot pool (2 MiB slots), torch "
+              f"index_select + index_copy_ (backend.py:40-44, :87-91), torch {torch.__version__} on {threads} threads")
+    return {
+        "metric": METRIC, "value": value, "unit": "slots/s", "n_gpus": dist.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": elapsed * 1e3 / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (bit copy)", "data": "synthetic (seeded)",
+        "impl": "reference",
+        "config": {"workload": "config4_copy", "pool_slots": 2 * slots + 1, "slots_per_step": slots,
+                   "ops_per_step": ["index_select", "index_copy_"], "num_v_heads": 32, "head_dim": 128,
+                   "parallelism": "rank 0 host CPU only"},
+        "cpu_baseline": {"value": value, "unit": "slots/s", "cores": threads, "kind": "reference", "sample": sample},
+        "e2e": {"value": value, "unit": "slots/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
 def run_reference(args, dist: Dist) -> dict | None:
     if dist.rank != 0:
         return None
@@ -855,9 +911,11 @@ def run_reference(args, dist: Dist) -> dict | None:
     if args.workload in ("decode_bf16", "verify_bf16"):
         return {"impl": "reference",
                 "unavailable": "the reference supports only an fp32 state pool (csrc/gdn_decode.cu:375-377)"}
+    if args.workload == "copy":
+        return reference_copy(args, dist)
     if args.workload not in ("decode", "verify"):
         return {"impl": "reference", "unavailable": f"the {args.workload} workload has no reference CPU arm in this "
-                                                    "harness (the decode and verify workloads do)"}
+                                                    "harness (the decode, verify and copy workloads do)"}
     device = torch.device("cuda", dist.local_rank) if torch.cuda.is_available() else torch.device("cpu")
     case = workloads.config2(device, seed=2) if args.workload == "decode" else workloads.config3(device, seed=3)
     threads = oracle.default_threads()

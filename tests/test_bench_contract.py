@@ -56,3 +56,14 @@ def test_reference_arm_without_a_cpu_path_says_so(workload):
                             check=True)
     line = json.loads(result.stdout.strip().splitlines()[-1])
     assert line["impl"] == "reference" and "unavailable" in line
+
+
+def test_reference_arm_times_config4_copies_on_the_host():
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    result = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--workload", "copy",
+                             "--steps", "3", "--warmup", "3"], capture_output=True, text=True, timeout=600, env=env,
+                            check=True)
+    line = json.loads(result.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["unit"] == "slots/s" and line["value"] > 0
+    assert line["config"]["workload"] == "config4_copy"
+    assert line["cpu_baseline"]["kind"] == "reference" and line["e2e"]["value"] == line["value"]

@@ -103,6 +103,7 @@ struct DecodeArgs {
   float eps;
   uint64_t wait_ns;   // bound of every in-kernel wait of the persistent kernel (ld_decode_wait_test)
   uint32_t extra_tx;  // test only: bytes each state load announces beyond what it copies (normally 0)
+  int64_t prefetch_stride;  // one-CTA-per-item kernel: blocks resident at once (0: no L2 prefetch)
 };
 
 // The state pool of a launch as the kernel's element type.
@@ -440,6 +441,27 @@ __global__ void __launch_bounds__(Tile<4>::kThreads, 2) gdn_decode_rowreg_kernel
   const int64_t head_offset = static_cast<int64_t>(head) * kHeadElems;
   float4 s[kRows][kVecPerRow];
   load_tile<kRows>(state_base<StateT>(p) + static_cast<int64_t>(src) * p.slot_stride + head_offset, g, j, s);
+
+  // The block one wave later most likely runs on this SM next: warm L2 with its source head now, so
+  // that its state load starts from L2 instead of HBM.  The last warp prepares no token.
+  if (warp == kThreads / 32 - 1 && lane == 0 && p.prefetch_stride > 0) {
+    const int64_t next = blockIdx.x + p.prefetch_stride;
+    if (next < p.total_items) {
+      const int next_request = static_cast<int>(next / HV);
+      const int next_head = static_cast<int>(next - static_cast<int64_t>(next_request) * HV);
+      const int next_acc = p.accepted[next_request];
+      const int next_src = (next_acc >= 1 && next_acc <= W) ? p.indices[next_request * W + next_acc - 1] : 0;
+      if (next_src > 0 && next_src < p.n_slots) {
+        const StateT* head = state_base<StateT>(p) + static_cast<int64_t>(next_src) * p.slot_stride +
+                             static_cast<int64_t>(next_head) * kHeadElems;
+        constexpr uint32_t kPiece = kHeadElems * sizeof(StateT) / 4;  // 16-byte multiple; heads are 16-byte aligned
+        for (int q = 0; q < 4; ++q) {
+          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(head + q * (kHeadElems / 4)), "r"(kPiece)
+                       : "memory");
+        }
+      }
+    }
+  }
 
   // Per-token activations: warp t prepares token t.
   if (warp < n) {
@@ -1426,6 +1448,7 @@ int prepare_decode(const void* qkv, int64_t qkv_row_stride, const void* a, int64
   args.eps = eps;
   args.wait_ns = g_wait_ns.load(std::memory_order_relaxed);
   args.extra_tx = g_extra_tx.load(std::memory_order_relaxed);
+  args.prefetch_stride = 0;
   return ok();
 }
 
@@ -1555,6 +1578,10 @@ extern "C" int ld_decode_bf16_state(const void* qkv, int64_t qkv_row_stride, con
     const bool vec_act = aligned(qkv, 8) && qkv_row_stride % 4 == 0 && aligned(gate, 8) &&
                          gate_row_stride % 4 == 0 && aligned(out, 8);
     const dim3 grid(static_cast<unsigned int>(args.total_items));
+    // Multi-token verify warms L2 with the next wave's states (two resident blocks per SM).
+    // Measured on B200, config 3: 71.7 -> 69.0 us on a bf16 pool; on an fp32 pool, whose launch is
+    // HBM-bound, the extra early reads cost 112.1 -> 117.6 us, so fp32 launches do not prefetch.
+    args.prefetch_stride = width > 1 ? 2 * static_cast<int64_t>(info.sms) : 0;
     err = vec_act ? ldb::launch(gdn_decode_rowreg_kernel<true, __nv_bfloat16>, grid, dim3(Tile<4>::kThreads), 0, s, 1,
                                 args)
                   : ldb::launch(gdn_decode_rowreg_kernel<false, __nv_bfloat16>, grid, dim3(Tile<4>::kThreads), 0, s,

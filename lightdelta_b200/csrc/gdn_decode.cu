@@ -385,6 +385,42 @@ __device__ __forceinline__ void gated_rmsnorm_store(const float* o_row, const fl
   store4_bf16<kVec>(out_row + 4 * lane, y);
 }
 
+__device__ __forceinline__ void l2_prefetch(const void* ptr, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ptr), "r"(bytes) : "memory");
+}
+
+// Warms L2 with what item `item` reads first: its source head and its tokens' q, k, v and gate rows.
+// Addresses come from the same validity rules as the item's own launch; anything invalid prefetches
+// nothing.
+template <typename StateT>
+__device__ void prefetch_item(const DecodeArgs& p, int64_t item) {
+  if (item >= p.total_items) return;
+  const int HV = p.num_v_heads;
+  const int W = p.width;
+  const int request = static_cast<int>(item / HV);
+  const int head = static_cast<int>(item - static_cast<int64_t>(request) * HV);
+  const int acc = p.accepted[request];
+  const int src = (acc >= 1 && acc <= W) ? p.indices[request * W + acc - 1] : 0;
+  if (src <= 0 || src >= p.n_slots) return;
+  // Heads are 16-byte aligned (pool base and slot stride are checked on the host).
+  const StateT* head_ptr =
+      state_base<StateT>(p) + static_cast<int64_t>(src) * p.slot_stride + static_cast<int64_t>(head) * kHeadElems;
+  for (int q = 0; q < 4; ++q) l2_prefetch(head_ptr + q * (kHeadElems / 4), kHeadElems * sizeof(StateT) / 4);
+  const int bos = p.cu[request];
+  const int n = p.cu[request + 1] - bos;
+  if (bos < 0 || n > W || static_cast<int64_t>(bos) + n > p.n_tokens) return;
+  const int H = p.num_k_heads;
+  const int key_head = head / p.heads_ratio;
+  for (int t = 0; t < n; ++t) {
+    const __nv_bfloat16* row = p.qkv + (bos + t) * p.qkv_row;
+    const __nv_bfloat16* rows[4] = {row + key_head * kDim, row + (H + key_head) * kDim, row + (2 * H + head) * kDim,
+                                    p.gate + (bos + t) * p.gate_row + head * kDim};
+    for (int r = 0; r < 4; ++r) {
+      if ((reinterpret_cast<uintptr_t>(rows[r]) & 15) == 0) l2_prefetch(rows[r], kRowBytes);
+    }
+  }
+}
+
 // ==========================================================================================
 // Fallback kernel: one CTA per item, state loaded straight into registers.
 // ==========================================================================================
@@ -442,25 +478,10 @@ __global__ void __launch_bounds__(Tile<4>::kThreads, 2) gdn_decode_rowreg_kernel
   float4 s[kRows][kVecPerRow];
   load_tile<kRows>(state_base<StateT>(p) + static_cast<int64_t>(src) * p.slot_stride + head_offset, g, j, s);
 
-  // The block one wave later most likely runs on this SM next: warm L2 with its source head now, so
-  // that its state load starts from L2 instead of HBM.  The last warp prepares no token.
+  // The block one wave later most likely runs on this SM next: warm L2 with its first reads now, so
+  // that they start from L2 instead of HBM.  The last warp prepares no token.
   if (warp == kThreads / 32 - 1 && lane == 0 && p.prefetch_stride > 0) {
-    const int64_t next = blockIdx.x + p.prefetch_stride;
-    if (next < p.total_items) {
-      const int next_request = static_cast<int>(next / HV);
-      const int next_head = static_cast<int>(next - static_cast<int64_t>(next_request) * HV);
-      const int next_acc = p.accepted[next_request];
-      const int next_src = (next_acc >= 1 && next_acc <= W) ? p.indices[next_request * W + next_acc - 1] : 0;
-      if (next_src > 0 && next_src < p.n_slots) {
-        const StateT* head = state_base<StateT>(p) + static_cast<int64_t>(next_src) * p.slot_stride +
-                             static_cast<int64_t>(next_head) * kHeadElems;
-        constexpr uint32_t kPiece = kHeadElems * sizeof(StateT) / 4;  // 16-byte multiple; heads are 16-byte aligned
-        for (int q = 0; q < 4; ++q) {
-          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(head + q * (kHeadElems / 4)), "r"(kPiece)
-                       : "memory");
-        }
-      }
-    }
+    prefetch_item<StateT>(p, blockIdx.x + p.prefetch_stride);
   }
 
   // Per-token activations: warp t prepares token t.
@@ -1578,9 +1599,11 @@ extern "C" int ld_decode_bf16_state(const void* qkv, int64_t qkv_row_stride, con
     const bool vec_act = aligned(qkv, 8) && qkv_row_stride % 4 == 0 && aligned(gate, 8) &&
                          gate_row_stride % 4 == 0 && aligned(out, 8);
     const dim3 grid(static_cast<unsigned int>(args.total_items));
-    // Multi-token verify warms L2 with the next wave's states (two resident blocks per SM).
-    // Measured on B200, config 3: 71.7 -> 69.0 us on a bf16 pool; on an fp32 pool, whose launch is
-    // HBM-bound, the extra early reads cost 112.1 -> 117.6 us, so fp32 launches do not prefetch.
+    // Multi-token verify warms L2 with the next wave's first reads (two resident blocks per SM).
+    // Measured on B200, config 3 on a bf16 pool: 71.7 us without, 69.0 us with the source heads,
+    // 66.0 us with the heads and the q / k / v / gate rows (70.5 us two waves ahead).  On an fp32
+    // pool, whose launch is HBM-bound, the heads cost 112.1 -> 117.6 us and the rows alone gain
+    // nothing measurable (111.6 -> 111.4 us), so fp32 launches do not prefetch.
     args.prefetch_stride = width > 1 ? 2 * static_cast<int64_t>(info.sms) : 0;
     err = vec_act ? ldb::launch(gdn_decode_rowreg_kernel<true, __nv_bfloat16>, grid, dim3(Tile<4>::kThreads), 0, s, 1,
                                 args)

@@ -14,9 +14,10 @@ kernel can run at the BASELINE geometry (H=16, HV=32).  It registers no torch op
 can share a process with lightdelta_b200.
 
 And it byte-compiles the reference's torch decode path -- python/lightdelta/__init__.py and
-python/lightdelta/reference/{__init__,gdn}.py, unmodified -- into sourceless .pyc files under
-oracle/_ref/py/lightdelta/ (an importable package for this interpreter), so that the reference's own
-CPU implementation can be timed on a host where the reference tree is absent (oracle/ref_torch.py).
+python/lightdelta/reference/{__init__,gdn}.py, unmodified -- into oracle/_ref/torch_path/, one
+"<module name>.bytecode" file each (the .pyc format under another name, loaded by
+oracle/ref_torch.py), so that the reference's own CPU implementation can be timed on a host where the
+reference tree is absent.
 
 Run here (where the reference sources exist):  python oracle/build_ref.py [--reference DIR]
 """
@@ -105,24 +106,28 @@ def build_harness(reference: Path = DEFAULT_REFERENCE, force: bool = False) -> P
     return HARNESS
 
 
-TORCH_PATH_DIR = OUT_DIR / "py"
-TORCH_PATH_MODULES = ("lightdelta/__init__.py", "lightdelta/reference/__init__.py", "lightdelta/reference/gdn.py")
+TORCH_PATH_DIR = OUT_DIR / "torch_path"
+# module name -> source under the reference's python/ directory, in the order they are loaded
+TORCH_PATH_MODULES = {
+    "lightdelta": "lightdelta/__init__.py",
+    "lightdelta.reference.gdn": "lightdelta/reference/gdn.py",
+    "lightdelta.reference": "lightdelta/reference/__init__.py",
+}
 
 
 def build_torch_path(reference: Path = DEFAULT_REFERENCE, force: bool = False) -> Path:
-    """Compiles the reference's torch path to bytecode, one .pyc beside where each source would be
-    (the layout Python imports without sources).  Only these three modules: the package marker and
-    post_conv_gdn, which import nothing of the reference beyond each other."""
+    """Compiles the reference's torch path to bytecode: the package marker and post_conv_gdn, which
+    import nothing of the reference beyond each other."""
     import py_compile
 
-    for module in TORCH_PATH_MODULES:
-        src = reference / "python" / module
+    TORCH_PATH_DIR.mkdir(parents=True, exist_ok=True)
+    for name, relative in TORCH_PATH_MODULES.items():
+        src = reference / "python" / relative
         if not src.exists():
             raise FileNotFoundError(f"reference module not found: {src}")
-        dst = TORCH_PATH_DIR / (module[: -len(".py")] + ".pyc")
+        dst = TORCH_PATH_DIR / f"{name}.bytecode"
         if dst.exists() and not force and src.stat().st_mtime <= dst.stat().st_mtime:
             continue
-        dst.parent.mkdir(parents=True, exist_ok=True)
         py_compile.compile(str(src), cfile=str(dst), doraise=True,
                            invalidation_mode=py_compile.PycInvalidationMode.UNCHECKED_HASH)
     return TORCH_PATH_DIR

@@ -1,8 +1,8 @@
 """The reference's own torch decode path on the host CPU -- TEST INFRASTRUCTURE ONLY.
 
 oracle/build_ref.py compiles the reference's python/lightdelta/reference package (post_conv_gdn,
-reference/gdn.py:70-128), unmodified, to bytecode under oracle/_ref/py/.  This module imports it
-from there and runs it the way GDNBackend's packed "torch_reference" mode does
+reference/gdn.py:70-128), unmodified, to bytecode under oracle/_ref/torch_path/.  This module loads
+it from there and runs it the way GDNBackend's packed "torch_reference" mode does
 (python/lightdelta/backend.py:30-91):
 
   1. each request's initial state is the pool slot of its last accepted step,
@@ -26,30 +26,42 @@ import sys
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-BYTECODE_DIR = HERE / "_ref" / "py"
+BYTECODE_DIR = HERE / "_ref" / "torch_path"
+# module name -> is a package, in load order (a module before the package that imports it)
+MODULES = (("lightdelta", True), ("lightdelta.reference.gdn", False), ("lightdelta.reference", True))
 
 _module = None
 
 
 def available() -> bool:
-    return (BYTECODE_DIR / "lightdelta" / "reference" / "gdn.pyc").exists()
+    return all((BYTECODE_DIR / f"{name}.bytecode").exists() for name, _ in MODULES)
 
 
 def reference():
     """The reference's lightdelta.reference package (GDNInputs, post_conv_gdn)."""
     global _module
     if _module is None:
+        import importlib.machinery
+        import importlib.util
+
         if not available():
             raise FileNotFoundError(f"{BYTECODE_DIR} holds no compiled reference: run python oracle/build_ref.py")
         loaded = sys.modules.get("lightdelta")
-        if loaded is not None and not str(getattr(loaded, "__file__", "")).startswith(str(BYTECODE_DIR)):
+        if loaded is not None and getattr(loaded, "__file__", None) != str(BYTECODE_DIR / "lightdelta.bytecode"):
             raise RuntimeError(f"another lightdelta package is already imported ({loaded.__file__})")
-        sys.path.insert(0, str(BYTECODE_DIR))
-        try:
-            import lightdelta.reference as module
-        finally:
-            sys.path.remove(str(BYTECODE_DIR))
-        _module = module
+        for name, package in MODULES:
+            if name in sys.modules:
+                continue
+            loader = importlib.machinery.SourcelessFileLoader(name, str(BYTECODE_DIR / f"{name}.bytecode"))
+            spec = importlib.util.spec_from_loader(name, loader, is_package=package)
+            module = importlib.util.module_from_spec(spec)
+            sys.modules[name] = module
+            try:
+                loader.exec_module(module)
+            except BaseException:
+                del sys.modules[name]
+                raise
+        _module = sys.modules["lightdelta.reference"]
     return _module
 
 

@@ -15,7 +15,7 @@ from lightdelta_b200 import workloads
 from oracle import ref_torch
 
 pytestmark = pytest.mark.skipif(not ref_torch.available(),
-                                reason="oracle/_ref/py not built (python oracle/build_ref.py, needs the reference)")
+                                reason="oracle/_ref/torch_path not built (python oracle/build_ref.py, needs the reference)")
 
 
 def _golden(name):

@@ -152,6 +152,26 @@ def test_invalid_requests_and_fault_word(device, kernel):
     check(case, host, "invalid requests")
 
 
+def test_invalid_requests_in_the_prefetched_wave(device):
+    """Multi-token launches on a bf16 pool warm L2 with the reads of the block one wave later
+    (blockIdx + 2 x SMs).  Invalid requests placed in that wave prefetch nothing out of range and
+    still decode as the oracle says."""
+    batch, width = 24, 4
+    case = bf16_case(batch, width, 1 + batch * width + 8, device=device, seed=81, accepted="uniform")
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    assert batch * case.num_v_heads > 2 * sms  # the first blocks prefetch the last requests' reads
+    slots = case.pool.shape[0]
+    case.accepted[batch - 4] = 0                                               # no accepted step
+    case.slots[batch - 3, int(case.accepted[batch - 3]) - 1] = slots + 7       # source slot out of range
+    case.slots[batch - 2, 2] = slots                                           # destination out of range
+    capi.fault_flags(clear=True)
+    host = to_numpy_case(case.kwargs())
+    run(case)
+    torch.cuda.synchronize()
+    assert capi.fault_flags(clear=True) == capi.LD_FAULT_DECODE_SLOT_RANGE
+    check(case, host, "invalid requests in the prefetched wave")
+
+
 def test_repeated_in_place_decode(device, kernel):
     """Three in-place steps: each re-reads the bf16 state the previous one stored."""
     case = bf16_case(16, 1, 40, device=device, seed=12)

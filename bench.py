@@ -431,7 +431,7 @@ def run_ours(args, dist: Dist) -> dict | None:
 
     e2e = None
     if args.workload in ("decode", "verify"):
-        e2e = run_e2e(case, args, dist, stream)
+        e2e = run_e2e(case, args, dist, stream, m["kernel_ms"] * 1000)
     cpu = cpu_torch = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline and args.workload in ("decode", "verify"):
         cpu = cpu_baseline(case, args.cpu_seconds)
@@ -526,14 +526,16 @@ def gpu_local_cpus(device_index: int):
         return None
 
 
-def run_e2e(case, args, dist: Dist, stream) -> dict:
+def run_e2e(case, args, dist: Dist, stream, kernel_us: float) -> dict:
     """Same metric through the public op with host buffers.  Every step copies its activations
     and request metadata from pinned host memory, runs torch.ops.lightdelta.decode and reads the
     output back to pinned host memory.  A step's inputs (the projection rows, the a/b rows, slots,
     cu and accepted counts) sit in one pinned staging buffer, so one copy carries them; the op
     reads views of the device copy.  Two buffer sets let the copies of one step overlap the
     kernel of the neighbouring step (H2D, compute and D2H on three streams); the state pool is
-    shared, so the kernels still run strictly in order."""
+    shared, so the kernels still run strictly in order.  After the timed region the same H2D and
+    D2H copies are timed alone (`copies_alone`): a step cannot be shorter than the slowest of them
+    and the kernel, so `bound` names which one sets the rate on this box."""
     import torch
 
     device = case.pool.device
@@ -615,11 +617,31 @@ def run_e2e(case, args, dist: Dist, stream) -> dict:
         torch.cuda.synchronize()
         dist.barrier()
         max_ms = dist.max(begin.elapsed_time(finish))
+
+        # After the timed region: the same copies alone (20 each, on their streams), so the line says
+        # what the host path of this box delivers and whether it or the kernel bounds a step.
+        def copy_us(stream_, dst, src):
+            first, last = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream_):
+                dst.copy_(src, non_blocking=True)
+                first.record(stream_)
+                for _ in range(20):
+                    dst.copy_(src, non_blocking=True)
+                last.record(stream_)
+            torch.cuda.synchronize()
+            return first.elapsed_time(last) * 1000 / 20
+
+        h2d_us = copy_us(s_in, dev[0], host[0])
+        d2h_us = copy_us(s_out, out_h[0], out_d[0])
     finally:
         os.sched_setaffinity(0, saved_affinity)
     return {"value": case.tokens * steps * dist.world / (max_ms * 1e-3), "unit": "tokens/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
             "ms_per_step": max_ms / steps, "host_enqueue_us_per_step": host_us,
+            "copies_alone": {"h2d_us": h2d_us, "h2d_gbs": h2d / (h2d_us * 1e3), "d2h_us": d2h_us,
+                             "d2h_gbs": d2h / (d2h_us * 1e3),
+                             "kernel_us": kernel_us,
+                             "bound": "host copies" if max(h2d_us, d2h_us) > kernel_us else "kernel"},
             "api": "torch.ops.lightdelta.decode; inputs from one pinned staging buffer per step (one H2D copy), "
                    "output to pinned memory; double-buffered so copies overlap the neighbouring step's kernel",
             "host_cpus": len(local) if local else None}

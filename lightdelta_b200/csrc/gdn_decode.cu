@@ -264,28 +264,39 @@ __device__ __forceinline__ void tile_step(float4 (&s)[kRows][kVecPerRow], const 
 
 // Writes the tile's row sets in the order kFirst, kFirst+1, ... (all indices compile-time, so the
 // tile stays in registers).
-template <int kRows, int kFirst>
+// kStream: streaming stores (st.global.cs; the stored states are not read again by this launch).
+template <int kRows, int kFirst, bool kStream>
 __device__ __forceinline__ void store_rows_from(float4* ptr, const float4 (&s)[kRows][kVecPerRow]) {
 #pragma unroll
   for (int step = 0; step < kRows; ++step) {
     const int i = (step + kFirst) % kRows;
 #pragma unroll
-    for (int c = 0; c < kVecPerRow; ++c) ptr[(i * Tile<kRows>::kRowGroups * kDim + c * 4 * kLanesPerRow) / 4] = s[i][c];
+    for (int c = 0; c < kVecPerRow; ++c) {
+      float4* at = &ptr[(i * Tile<kRows>::kRowGroups * kDim + c * 4 * kLanesPerRow) / 4];
+      if constexpr (kStream) {
+        __stcs(at, s[i][c]);
+      } else {
+        *at = s[i][c];
+      }
+    }
   }
 }
 
 // Stores a register tile to one head's state.  CTAs start at different row sets (blockIdx.x mod
 // kRows): when every SM writes the same quarter of its head at the same moment the state writes
 // concentrate on part of the memory system; staggering them measured 5-7% faster on B200.
-template <int kRows>
+// Measured on B200 (config 3, back to back): streaming stores take the one-CTA-per-item verify
+// kernel from 112.6 to 111.1 us on an fp32 pool and from 66.2 to 65.3 us on a bf16 pool; the
+// persistent fp32 decode kernel keeps plain stores (176.7 -> 177.7 us with them).
+template <int kRows, bool kStream = false>
 __device__ __forceinline__ void store_tile(float* dst_head, int g, int j, const float4 (&s)[kRows][kVecPerRow]) {
   float4* ptr = reinterpret_cast<float4*>(dst_head + g * kDim + 4 * j);
   static_assert(kRows <= 4, "rotation covers at most four row sets");
   switch (blockIdx.x % kRows) {
-    case 0: store_rows_from<kRows, 0>(ptr, s); break;
-    case 1: store_rows_from<kRows, 1 % kRows>(ptr, s); break;
-    case 2: store_rows_from<kRows, 2 % kRows>(ptr, s); break;
-    default: store_rows_from<kRows, 3 % kRows>(ptr, s); break;
+    case 0: store_rows_from<kRows, 0, kStream>(ptr, s); break;
+    case 1: store_rows_from<kRows, 1 % kRows, kStream>(ptr, s); break;
+    case 2: store_rows_from<kRows, 2 % kRows, kStream>(ptr, s); break;
+    default: store_rows_from<kRows, 3 % kRows, kStream>(ptr, s); break;
   }
 }
 
@@ -336,7 +347,7 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-template <int kRows, int kFirst>
+template <int kRows, int kFirst, bool kStream>
 __device__ __forceinline__ void store_rows_from(__nv_bfloat16* base, const float4 (&s)[kRows][kVecPerRow]) {
 #pragma unroll
   for (int step = 0; step < kRows; ++step) {
@@ -345,20 +356,26 @@ __device__ __forceinline__ void store_rows_from(__nv_bfloat16* base, const float
     for (int h = 0; h < kVecPerRow / 2; ++h) {
       const float4& a = s[i][2 * h];
       const float4& b = s[i][2 * h + 1];
-      *reinterpret_cast<uint4*>(base + i * Tile<kRows>::kRowGroups * kDim + 64 * h) =
+      uint4* at = reinterpret_cast<uint4*>(base + i * Tile<kRows>::kRowGroups * kDim + 64 * h);
+      const uint4 words =
           make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(b.x, b.y), pack_bf16x2(b.z, b.w));
+      if constexpr (kStream) {
+        __stcs(at, words);
+      } else {
+        *at = words;
+      }
     }
   }
 }
 
-template <int kRows>
+template <int kRows, bool kStream = false>
 __device__ __forceinline__ void store_tile(__nv_bfloat16* dst_head, int g, int j, const float4 (&s)[kRows][kVecPerRow]) {
   __nv_bfloat16* base = dst_head + g * kDim + 8 * j;
   switch (blockIdx.x % kRows) {
-    case 0: store_rows_from<kRows, 0>(base, s); break;
-    case 1: store_rows_from<kRows, 1 % kRows>(base, s); break;
-    case 2: store_rows_from<kRows, 2 % kRows>(base, s); break;
-    default: store_rows_from<kRows, 3 % kRows>(base, s); break;
+    case 0: store_rows_from<kRows, 0, kStream>(base, s); break;
+    case 1: store_rows_from<kRows, 1 % kRows, kStream>(base, s); break;
+    case 2: store_rows_from<kRows, 2 % kRows, kStream>(base, s); break;
+    default: store_rows_from<kRows, 3 % kRows, kStream>(base, s); break;
   }
 }
 
@@ -547,7 +564,8 @@ __global__ void __launch_bounds__(Tile<4>::kThreads, 2) gdn_decode_rowreg_kernel
     }
     const int dst = sh_dst[t];
     if (dst > 0) {
-      store_tile<kRows>(state_base<StateT>(p) + static_cast<int64_t>(dst) * p.slot_stride + head_offset, g, j, s);
+      store_tile<kRows, true>(state_base<StateT>(p) + static_cast<int64_t>(dst) * p.slot_stride + head_offset, g, j,
+                              s);
     }
   }
   __syncthreads();
@@ -600,6 +618,7 @@ struct Smem {
   using State = float;
   static constexpr int kStateStages = kStates;
   static constexpr int kActStages = kStateStages + 1;
+  static constexpr bool kStatesReadOnce = false;  // plain state loads (evict-first: 176.7 -> 178.3 us)
   float state[kStateStages][kHeadElems];
   ActStage act[kActStages];
   float out[2][kMaxTokens][kDim];
@@ -655,6 +674,17 @@ __device__ __noinline__ bool mbar_wait(unsigned long long* bar, uint32_t parity,
     if (global_ns() - start > limit_ns) return false;
   }
   return true;
+}
+
+// The same with an L2 evict-first policy, for data read once.
+__device__ __forceinline__ void bulk_load_once(void* dst, const void* src, uint32_t bytes, unsigned long long* bar) {
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
 }
 
 // TMA bulk copy global -> this CTA's own shared memory (one destination), completing on `bar`.
@@ -835,8 +865,13 @@ __device__ void produce(const DecodeArgs& p, S& sm, int lane) {
         // Four pieces, starting at a per-SM quarter (see store_tile).
         for (int q = 0; q < 4; ++q) {
           const int piece = (q + static_cast<int>(blockIdx.x)) & 3;
-          bulk_load(sm.state[s] + piece * (kHeadElems / 4), src_head + piece * (kHeadElems / 4), kStateBytes / 4,
-                    &sm.full[s]);
+          if constexpr (S::kStatesReadOnce) {
+            bulk_load_once(sm.state[s] + piece * (kHeadElems / 4), src_head + piece * (kHeadElems / 4),
+                           kStateBytes / 4, &sm.full[s]);
+          } else {
+            bulk_load(sm.state[s] + piece * (kHeadElems / 4), src_head + piece * (kHeadElems / 4), kStateBytes / 4,
+                      &sm.full[s]);
+          }
         }
         const int key_head = head / p.heads_ratio;
         for (int t = 0; t < n; ++t) {
@@ -1081,6 +1116,9 @@ struct Smem {
   using State = __nv_bfloat16;
   static constexpr int kStateStages = 6;
   static constexpr int kActStages = 8;
+  // State loads with an L2 evict-first policy and streaming state stores (RowWords::store): 95.6 ->
+  // 93.8 us on config 2 (B200); either alone measured 95.7 (stores) and 96.2 us (loads).
+  static constexpr bool kStatesReadOnce = true;
   __nv_bfloat16 state[kStateStages][kHeadElems];
   ActStage1 act[kActStages];
   float out[kGroups][2][kDim];
@@ -1158,9 +1196,10 @@ struct RowWords {
     return (acc_a.x + acc_a.y) + (acc_b.x + acc_b.y);
   }
 
+  // Streaming stores (st.global.cs), with the evict-first state loads of this kernel's ring.
   __device__ __forceinline__ void store(__nv_bfloat16* row) const {
-    *reinterpret_cast<uint4*>(row) = w[0];
-    *reinterpret_cast<uint4*>(row + 64) = w[1];
+    __stcs(reinterpret_cast<uint4*>(row), w[0]);
+    __stcs(reinterpret_cast<uint4*>(row + 64), w[1]);
   }
 };
 

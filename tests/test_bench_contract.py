@@ -67,3 +67,22 @@ def test_reference_arm_times_config4_copies_on_the_host():
     assert line["impl"] == "reference" and line["unit"] == "slots/s" and line["value"] > 0
     assert line["config"]["workload"] == "config4_copy"
     assert line["cpu_baseline"]["kind"] == "reference" and line["e2e"]["value"] == line["value"]
+
+
+def test_reference_arm_under_torchrun_prints_one_line_from_rank_zero():
+    """The launch the driver uses for N > 1: rank 0 alone runs and prints the reference line, the
+    other ranks exit 0 without work."""
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    result = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                             "--master-addr", "127.0.0.1", "--master-port", str(port), str(ROOT / "bench.py"),
+                             "--impl", "reference", "--gpus", "2", "--steps", "3", "--warmup", "3",
+                             "--cpu-seconds", "1"], capture_output=True, text=True, timeout=600, env=env, check=True)
+    lines = [line for line in result.stdout.splitlines() if line.strip().startswith("{")]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    assert line["impl"] == "reference" and line["value"] > 0 and line["n_gpus"] == 2

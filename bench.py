@@ -713,7 +713,8 @@ def torch_reference_baseline(case, seconds: float, requests: int | None = None) 
     from oracle import ref_torch
 
     if not ref_torch.available():
-        return {"unavailable": "oracle/_ref/torch_path not built (python oracle/build_ref.py, where the reference exists)"}
+        return {"unavailable": "oracle/_ref/torch_path not built (python oracle/build_ref.py where the reference "
+                               "exists)"}
     w = host_workload(case, requests)
     saved_threads = torch.get_num_threads()
     torch.set_num_threads(oracle.default_threads())

@@ -14,8 +14,9 @@ from helpers import assert_out_close, assert_state_close, backend_torch, bits, t
 from lightdelta_b200 import workloads
 from oracle import ref_torch
 
-pytestmark = pytest.mark.skipif(not ref_torch.available(),
-                                reason="oracle/_ref/torch_path not built (python oracle/build_ref.py, needs the reference)")
+pytestmark = pytest.mark.skipif(
+    not ref_torch.available(),
+    reason="oracle/_ref/torch_path not built (python oracle/build_ref.py, needs the reference)")
 
 
 def _golden(name):

@@ -702,22 +702,16 @@ def cpu_baseline(case, seconds: float) -> dict:
                       f"{elapsed:.1f} s, C oracle with OpenMP"}
 
 
-def torch_reference_baseline(case, seconds: float, requests: int | None = None) -> dict:
-    """The reference's own CPU implementation (oracle/ref_torch.py: its post_conv_gdn, compiled
-    unmodified, with GDNBackend's packed gather and commit) on the same host workload as the C port,
-    repeated for ~`seconds` on every host thread this process may use."""
+def _torch_reference_step(case, requests: int | None = None):
+    """One step of the reference's own CPU implementation (oracle/ref_torch.py: its post_conv_gdn,
+    compiled unmodified, with GDNBackend's packed gather and commit) on a host copy of `case`
+    (the C port's host workload), and that workload."""
     import numpy as np
     import torch
 
-    import oracle
     from oracle import ref_torch
 
-    if not ref_torch.available():
-        return {"unavailable": "oracle/_ref/torch_path not built (python oracle/build_ref.py where the reference "
-                               "exists)"}
     w = host_workload(case, requests)
-    saved_threads = torch.get_num_threads()
-    torch.set_num_threads(oracle.default_threads())
 
     def bf16(x):
         return torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).view(torch.bfloat16)
@@ -731,6 +725,26 @@ def torch_reference_baseline(case, seconds: float, requests: int | None = None) 
     def step():
         ref_torch.packed_decode(**args, num_k_heads=w["num_k_heads"])
 
+    return step, w
+
+
+TORCH_UNAVAILABLE = {"unavailable": "oracle/_ref/torch_path not built (python oracle/build_ref.py where the "
+                                    "reference exists)"}
+
+
+def torch_reference_baseline(case, seconds: float, requests: int | None = None) -> dict:
+    """The reference's own CPU implementation on the same host workload as the C port, repeated for
+    ~`seconds` on every host thread this process may use."""
+    import torch
+
+    import oracle
+    from oracle import ref_torch
+
+    if not ref_torch.available():
+        return dict(TORCH_UNAVAILABLE)
+    step, w = _torch_reference_step(case, requests)
+    saved_threads = torch.get_num_threads()
+    torch.set_num_threads(oracle.default_threads())
     try:
         step()  # warm-up
         reps, t0 = 0, time.perf_counter()
@@ -747,6 +761,43 @@ def torch_reference_baseline(case, seconds: float, requests: int | None = None) 
             "sample": f"{w['requests']} sequences ({w['tokens']} tokens) per step x {reps} steps, {elapsed:.1f} s, "
                       f"the reference's post_conv_gdn (python/lightdelta/reference/gdn.py:70-128) with "
                       f"GDNBackend's packed gather and commit (backend.py:30-91), torch {torch.__version__} CPU"}
+
+
+def torch_reference_configs(device, runs: int = 5) -> dict:
+    """BASELINE configs 1-3 through the reference's own CPU implementation, each the median of `runs`
+    timed steps after one warm-up, on every host thread this process may use."""
+    import statistics
+
+    import torch
+
+    import oracle
+    from lightdelta_b200 import workloads
+    from oracle import ref_torch
+
+    if not ref_torch.available():
+        return dict(TORCH_UNAVAILABLE)
+    cases = (("config1", lambda: workloads.make_decode_case(1, 1, 2, device=device, seed=1)),
+             ("config2", lambda: workloads.config2(device, seed=2)),
+             ("config3", lambda: workloads.config3(device, seed=3)))
+    saved_threads = torch.get_num_threads()
+    torch.set_num_threads(oracle.default_threads())
+    result = {}
+    try:
+        for name, build in cases:
+            step, w = _torch_reference_step(build())
+            step()  # warm-up
+            times = []
+            for _ in range(runs):
+                t0 = time.perf_counter()
+                step()
+                times.append(time.perf_counter() - t0)
+            median = statistics.median(times)
+            result[name] = {"tokens_per_s": w["tokens"] / median, "median_ms": median * 1e3, "runs": runs,
+                            "sequences": w["requests"], "tokens": w["tokens"]}
+        result.update(cores=torch.get_num_threads(), torch=torch.__version__, kind="reference")
+    finally:
+        torch.set_num_threads(saved_threads)
+    return result
 
 
 def unfused_conv_decode_us(case, conv, stream) -> dict | None:
@@ -981,6 +1032,7 @@ def run_reference(args, dist: Dist) -> dict | None:
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "reference_torch": torch_reference_baseline(case, args.cpu_seconds),
+        "reference_torch_configs": torch_reference_configs(device),
         "reference_gpu_kernel": reference_gpu_kernel(args.steps, args.warmup),
     }
 

@@ -43,6 +43,10 @@ def test_reference_arm_prints_one_contract_line():
     torch_path = line["reference_torch"]
     if "unavailable" not in torch_path:
         assert torch_path["kind"] == "reference" and torch_path["value"] > 0 and torch_path["cores"] >= 1
+        configs = line["reference_torch_configs"]
+        assert configs["cores"] >= 1 and configs["torch"]
+        for name in ("config1", "config2", "config3"):
+            assert configs[name]["runs"] >= 5 and configs[name]["tokens_per_s"] > 0
     assert line["e2e"] == {"value": line["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
     assert line["config"]["workload"] == "config2_decode"

@@ -213,6 +213,27 @@ def test_invalid_requests_and_fault_word(device, kernel):
     assert_state_close(case.pool.cpu().numpy(), host["pool"], "invalid requests pool")
 
 
+def test_one_token_launch_with_padding_requests(device, kernel):
+    """One-token decode with padding requests (no tokens: cu repeats, as in a batch padded to a
+    captured size) at a size where `auto` picks the streaming kernel (320 x 32 items)."""
+    batch = 320
+    case = workloads.make_decode_case(batch, 1, batch + 8, device=device, seed=31)
+    live = torch.ones(batch, dtype=torch.int32)
+    live[3::4] = 0
+    cu = torch.zeros(batch + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(live, 0)
+    case.cu.copy_(cu.to(device))
+    case.out.fill_(1.0)
+    capi.fault_flags(clear=True)
+    host = to_numpy_case(case.kwargs())
+    capi.decode(*case.op_args())
+    torch.cuda.synchronize()
+    assert capi.fault_flags(clear=True) == 0
+    run_oracle(host, case.num_k_heads)
+    assert_out_close(bits(case.out), host["out"], "padding requests out")
+    assert_state_close(case.pool.cpu().numpy(), host["pool"], "padding requests pool")
+
+
 def test_too_many_tokens_sets_the_token_fault(device, kernel):
     case = workloads.make_decode_case(2, 2, 8, device=device, seed=6)
     capi.fault_flags(clear=True)

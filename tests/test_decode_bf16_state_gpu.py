@@ -172,6 +172,25 @@ def test_invalid_requests_in_the_prefetched_wave(device):
     check(case, host, "invalid requests in the prefetched wave")
 
 
+def test_one_token_launch_with_padding_requests(device, kernel):
+    """Padding requests (no tokens: cu repeats) in a one-token launch large enough for `auto` to pick
+    the two-group streaming kernel (320 x 32 items)."""
+    batch = 320
+    case = bf16_case(batch, 1, batch + 8, device=device, seed=32)
+    live = torch.ones(batch, dtype=torch.int32)
+    live[3::4] = 0
+    cu = torch.zeros(batch + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(live, 0)
+    case.cu.copy_(cu.to(device))
+    case.out.fill_(1.0)
+    capi.fault_flags(clear=True)
+    host = to_numpy_case(case.kwargs())
+    run(case)
+    torch.cuda.synchronize()
+    assert capi.fault_flags(clear=True) == 0
+    check(case, host, "padding requests")
+
+
 def test_repeated_in_place_decode(device, kernel):
     """Three in-place steps: each re-reads the bf16 state the previous one stored."""
     case = bf16_case(16, 1, 40, device=device, seed=12)
